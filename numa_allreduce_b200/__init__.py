@@ -1,0 +1,39 @@
+"""numa_allreduce_b200: a Blackwell-native intra-node allreduce library.
+
+Public API (parity with the reference's ``src/__init__.py``, which exported
+``NumaAwareAllReduce`` and ``NumaTopology``):
+
+* :class:`NumaAwareAllReduce`: custom allreduce over NVLink 5 / NVSwitch with
+  one-shot, two-shot, NVLink SHARP and hierarchical (NUMA-grouped) protocols,
+  CUDA-graph buffer registration and bounded device waits;
+* :class:`NumaTopology`, :class:`NumaNodeInfo`, :class:`GpuNumaInfo`,
+  :func:`detect_numa_topology`: NUMA and GPU topology detection;
+* :class:`HierSchedule` and :func:`emulate_allreduce`: the schedule and its
+  gloo/CPU executor;
+* :func:`fused_allreduce_rmsnorm`, :func:`rmsnorm_residual`: the fused TP
+  layer tail.
+"""
+
+from .ops.fused import fused_allreduce_rmsnorm, rmsnorm_residual
+from .parallel.comm import AllReduceError, NumaAwareAllReduce
+from .parallel.emulate import emulate_allreduce
+from .parallel.schedule import HierSchedule, reference_allreduce
+from .parallel.select import AlgoSelector
+from .utils.topology import GpuNumaInfo, NumaNodeInfo, NumaTopology, detect_numa_topology
+
+__all__ = [
+    "AlgoSelector",
+    "AllReduceError",
+    "GpuNumaInfo",
+    "HierSchedule",
+    "NumaAwareAllReduce",
+    "NumaNodeInfo",
+    "NumaTopology",
+    "detect_numa_topology",
+    "emulate_allreduce",
+    "fused_allreduce_rmsnorm",
+    "reference_allreduce",
+    "rmsnorm_residual",
+]
+
+__version__ = "0.1.0"

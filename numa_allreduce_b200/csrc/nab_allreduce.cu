@@ -1,0 +1,493 @@
+// Allreduce kernels for B200 over NVLink 5 / NVSwitch, and their launcher.
+//
+// Every kernel reduces in fp32 in ascending rank order and rounds once, so all
+// ranks produce bit-identical results and a CPU fp32 sum in rank order is an
+// exact oracle.
+//
+// Protocols (capability parity with the reference's effective kernel, vLLM's
+// one-/two-shot custom allreduce reached through ops.all_reduce in
+// src/numa_all_reduce.py:354-357, and with its dead three-stage kernels in
+// src/numa_all_reduce.cu:228-344):
+//   oneshot       push the whole input into every peer's slot (double
+//                 buffered by call parity), one flag exchange, every rank
+//                 reduces everything. No end barrier.
+//   twoshot       tiled rounds per CTA: push chunk j to owner j (reduce-
+//                 scatter by stores), owner reduces, peers pull the result
+//                 (all-gather by loads). Workspace is independent of message
+//                 size; no start or end barrier.
+//   hier          the reference's three stages done right: intra-group RS,
+//                 exchange of partial sums between same-slice owners of other
+//                 groups, intra-group AG.
+//   oneshot_pull  registered inputs (CUDA-graph path): read peers' buffers
+//                 in place between a start and an end barrier.
+//   nvls_oneshot  copy into the multicast-bound workspace, one arrival
+//                 counter, multimem.ld_reduce of the whole message.
+//   nvls_twoshot  tiled rounds: copy in, multimem.ld_reduce own chunk,
+//                 multimem.st of the result to every GPU, copy out.
+//   copy          world size 1.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+
+#include "nab_device.cuh"
+#include "nab_kernels.h"
+#include "nab_params.h"
+#include "nab_proto.cuh"
+
+namespace nab {
+
+namespace {
+
+constexpr int kThreads = 512;
+
+NAB_DINLINE SignalPad* pad_of(const RankView& me, int r) { return pad_at(me.wsp, r); }
+
+NAB_DINLINE uint32_t begin_call(const RankView& me) { return ::nab::begin_call(me.wsp, me.rank); }
+
+NAB_DINLINE void end_call(const RankView& me, uint32_t epoch) { ::nab::end_call(me.wsp, me.rank, epoch); }
+
+NAB_DINLINE WaitCtx make_wait(const ARParams& p, const RankView& me, uint32_t epoch) {
+  return ::nab::make_wait(p.err, p.err_host, p.timeout_ns, me.wsp, me.rank, epoch);
+}
+
+NAB_DINLINE bool exchange(const RankView& me, int kind, int slot, uint64_t seq, const int* peers,
+                          int npeers, const WaitCtx& w, uint32_t stage) {
+  return ::nab::exchange(me.wsp, me.rank, kind, slot, seq, peers, npeers, w, stage);
+}
+
+// ------------------------------------------------------------------ copy ----
+__global__ void __launch_bounds__(kThreads) k_copy(const __grid_constant__ ARParams p) {
+  const RankView& me = p.v[blockIdx.y];
+  const uint4* src = reinterpret_cast<const uint4*>(me.in);
+  uint4* dst = reinterpret_cast<uint4*>(me.out);
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  for (; i + 3 * stride < p.npacks; i += 4 * stride) {
+    uint4 a = ld_plain(src + i), b = ld_plain(src + i + stride);
+    uint4 c = ld_plain(src + i + 2 * stride), d = ld_plain(src + i + 3 * stride);
+    st_plain(dst + i, a);
+    st_plain(dst + i + stride, b);
+    st_plain(dst + i + 2 * stride, c);
+    st_plain(dst + i + 3 * stride, d);
+  }
+  for (; i < p.npacks; i += stride) st_plain(dst + i, ld_plain(src + i));
+}
+
+// --------------------------------------------------------------- oneshot ----
+template <typename T, int WS>
+__global__ void __launch_bounds__(kThreads) k_oneshot(const __grid_constant__ ARParams p) {
+  const RankView& me = p.v[blockIdx.y];
+  const int rank = me.rank;
+  const uint32_t epoch = begin_call(me);
+  const WaitCtx w = make_wait(p, me, epoch);
+  const int parity = epoch & 1;
+  const int64_t per = ceil_div<int64_t>(p.npacks, gridDim.x);
+  const int64_t beg = per * blockIdx.x;
+  const int64_t end = min(p.npacks, beg + per);
+  const uint4* src = reinterpret_cast<const uint4*>(me.in);
+  const int64_t slot_packs = p.L.oneshot_max / 16;
+  auto slot = [&](int owner_rank, int src_rank) -> uint4* {
+    return reinterpret_cast<uint4*>(me.wsp[owner_rank] + p.L.oneshot_off) +
+           (static_cast<int64_t>(parity) * WS + src_rank) * slot_packs;
+  };
+  // 1. push my input into slot [rank] of every peer
+  for (int64_t i = beg + threadIdx.x; i < end; i += blockDim.x) {
+    const uint4 x = ld_plain(src + i);
+#pragma unroll
+    for (int k = 1; k < WS; ++k) st_plain(slot((rank + k) % WS, rank) + i, x);
+  }
+  int peers[WS > 1 ? WS - 1 : 1];
+  all_peers<WS>(rank, peers);
+  const bool ok = exchange(me, kFlagOneshot, blockIdx.x, make_seq(epoch, 0), peers, WS - 1, w,
+                           kStageOneshot);
+  // 2. reduce all WS contributions in rank order
+  if (ok) {
+    uint4* dst = reinterpret_cast<uint4*>(me.out);
+    for (int64_t i = beg + threadIdx.x; i < end; i += blockDim.x) {
+      uint4 x[WS];
+#pragma unroll
+      for (int q = 0; q < WS; ++q) x[q] = (q == rank) ? ld_plain(src + i) : ld_cg(slot(rank, q) + i);
+      Acc<T> a;
+      acc_set(a, x[0]);
+#pragma unroll
+      for (int q = 1; q < WS; ++q) acc_add(a, x[q]);
+      st_plain(dst + i, acc_pack(a));
+    }
+  }
+  end_call(me, epoch);
+}
+
+// --------------------------------------------------------------- twoshot ----
+template <typename T, int WS>
+__global__ void __launch_bounds__(kThreads) k_twoshot(const __grid_constant__ ARParams p) {
+  const RankView& me = p.v[blockIdx.y];
+  const int rank = me.rank;
+  const uint32_t epoch = begin_call(me);
+  const WaitCtx w = make_wait(p, me, epoch);
+  const int c = blockIdx.x;
+  const int chp = p.chunk_packs;
+  const int64_t tile = static_cast<int64_t>(WS) * chp;
+  const int64_t stripe = tile * gridDim.x;
+  const int64_t cta_packs = (WS + 1) * (p.L.chunk_max / 16);
+  const uint4* src = reinterpret_cast<const uint4*>(me.in);
+  uint4* dst = reinterpret_cast<uint4*>(me.out);
+  // CTA c's region in rank r's workspace: [WS rs slots][result]
+  auto region = [&](int r) -> uint4* {
+    return reinterpret_cast<uint4*>(me.wsp[r] + p.L.twoshot_off) + c * cta_packs;
+  };
+  const int64_t slot_stride = p.L.chunk_max / 16;
+  int peers[WS - 1];
+  all_peers<WS>(rank, peers);
+  bool ok = true;
+  for (int r = 0; r < p.rounds && ok; ++r) {
+    const int64_t tbase = r * stripe + c * tile;
+    const uint64_t seq = make_seq(epoch, r + 1);
+    // 1. reduce-scatter by stores: chunk j -> owner j, slot [rank]
+    for (int i = threadIdx.x; i < chp; i += blockDim.x) {
+      uint4 x[WS - 1];
+#pragma unroll
+      for (int k = 0; k < WS - 1; ++k) {
+        const int64_t g = tbase + static_cast<int64_t>(peers[k]) * chp + i;
+        if (g < p.npacks) x[k] = ld_plain(src + g);
+      }
+#pragma unroll
+      for (int k = 0; k < WS - 1; ++k) {
+        const int64_t g = tbase + static_cast<int64_t>(peers[k]) * chp + i;
+        if (g < p.npacks) st_plain(region(peers[k]) + rank * slot_stride + i, x[k]);
+      }
+    }
+    ok = exchange(me, kFlagRS, c, seq, peers, WS - 1, w, kStageRS);
+    if (!ok) break;
+    // 2. reduce my chunk; publish it in my result slot and in my output
+    uint4* mine = region(rank);
+    for (int i = threadIdx.x; i < chp; i += blockDim.x) {
+      const int64_t g = tbase + static_cast<int64_t>(rank) * chp + i;
+      if (g < p.npacks) {
+        uint4 x[WS];
+#pragma unroll
+        for (int q = 0; q < WS; ++q) x[q] = (q == rank) ? ld_plain(src + g) : ld_cg(mine + q * slot_stride + i);
+        Acc<T> a;
+        acc_set(a, x[0]);
+#pragma unroll
+        for (int q = 1; q < WS; ++q) acc_add(a, x[q]);
+        const uint4 y = acc_pack(a);
+        st_plain(mine + WS * slot_stride + i, y);
+        st_plain(dst + g, y);
+      }
+    }
+    ok = exchange(me, kFlagAG, c, seq, peers, WS - 1, w, kStageAG);
+    if (!ok) break;
+    // 3. all-gather by loads from every owner's result slot
+    for (int i = threadIdx.x; i < chp; i += blockDim.x) {
+      uint4 x[WS - 1];
+#pragma unroll
+      for (int k = 0; k < WS - 1; ++k) {
+        const int64_t g = tbase + static_cast<int64_t>(peers[k]) * chp + i;
+        if (g < p.npacks) x[k] = ld_cg(region(peers[k]) + WS * slot_stride + i);
+      }
+#pragma unroll
+      for (int k = 0; k < WS - 1; ++k) {
+        const int64_t g = tbase + static_cast<int64_t>(peers[k]) * chp + i;
+        if (g < p.npacks) st_plain(dst + g, x[k]);
+      }
+    }
+  }
+  end_call(me, epoch);
+}
+
+// ------------------------------------------------------------------ hier ----
+// Stage 1: reduce-scatter inside the group (chunk l -> local index l).
+// Stage 2: the owners of chunk l in all groups exchange their partial sums
+//          (double-buffered by the CTA's global round parity) and each adds
+//          them in group order.
+// Stage 3: all-gather inside the group by loads.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) k_hier(const __grid_constant__ ARParams p) {
+  const RankView& me = p.v[blockIdx.y];
+  const int rank = me.rank;
+  const uint32_t epoch = begin_call(me);
+  const WaitCtx w = make_wait(p, me, epoch);
+  const int c = blockIdx.x;
+  const int G = p.gsize, NG = p.ngroups;
+  const int g = p.group_of[rank], l = p.lidx_of[rank];
+  const int chp = p.chunk_packs;
+  const int64_t tile = static_cast<int64_t>(G) * chp;
+  const int64_t stripe = tile * gridDim.x;
+  const int64_t slot_stride = p.L.chunk_max / 16;
+  const int64_t cta_packs = (G + 2 * NG + 1) * slot_stride;
+  const uint4* src = reinterpret_cast<const uint4*>(me.in);
+  uint4* dst = reinterpret_cast<uint4*>(me.out);
+  auto region = [&](int r) -> uint4* {
+    return reinterpret_cast<uint4*>(me.wsp[r] + p.L.hier_off) + c * cta_packs;
+  };
+  // slots: [0,G) rs by source local index, [G, G+2NG) x by parity*NG + source
+  // group, [G+2NG] result.
+  int gpeers[kMaxRanks], xpeers[kMaxRanks];
+  int ng = 0, nx = 0;
+  for (int m = 0; m < G; ++m)
+    if (m != l) gpeers[ng++] = p.member[g][m];
+  for (int h = 0; h < NG; ++h)
+    if (h != g) xpeers[nx++] = p.member[h][l];
+  __shared__ uint32_t s_base;
+  if (threadIdx.x == 0) s_base = ld_volatile_u32(&pad_of(me, rank)->hier_rounds[c]);
+  __syncthreads();
+  const uint32_t base_rounds = s_base;
+  bool ok = true;
+  int r = 0;
+  for (; r < p.rounds && ok; ++r) {
+    const int64_t tbase = r * stripe + c * tile;
+    const uint64_t seq = make_seq(epoch, r + 1);
+    const int par = (base_rounds + r) & 1;
+    // 1. intra-group reduce-scatter by stores
+    for (int i = threadIdx.x; i < chp; i += blockDim.x) {
+      for (int m = 0; m < G; ++m) {
+        if (m == l) continue;
+        const int64_t gi = tbase + static_cast<int64_t>(m) * chp + i;
+        if (gi < p.npacks) st_plain(region(p.member[g][m]) + l * slot_stride + i, ld_plain(src + gi));
+      }
+    }
+    ok = exchange(me, kFlagHierRS, c, seq, gpeers, ng, w, kStageRS);
+    if (!ok) break;
+    // 2a. group partial of chunk l -> my own x slot and the same-slice owners
+    uint4* mine = region(rank);
+    for (int i = threadIdx.x; i < chp; i += blockDim.x) {
+      const int64_t gi = tbase + static_cast<int64_t>(l) * chp + i;
+      if (gi < p.npacks) {
+        Acc<T> a;
+        for (int m = 0; m < G; ++m) {
+          const uint4 x = (m == l) ? ld_plain(src + gi) : ld_cg(mine + m * slot_stride + i);
+          if (m == 0) acc_set(a, x); else acc_add(a, x);
+        }
+        const uint4 part = acc_pack(a);
+        const int64_t xs = (G + par * NG + g) * slot_stride + i;
+        st_plain(mine + xs, part);
+        for (int h = 0; h < NG; ++h)
+          if (h != g) st_plain(region(p.member[h][l]) + xs, part);
+      }
+    }
+    ok = exchange(me, kFlagHierX, c, seq, xpeers, nx, w, kStageHierX);
+    if (!ok) break;
+    // 2b. sum the group partials in group order -> result slot and output
+    for (int i = threadIdx.x; i < chp; i += blockDim.x) {
+      const int64_t gi = tbase + static_cast<int64_t>(l) * chp + i;
+      if (gi < p.npacks) {
+        Acc<T> a;
+        for (int h = 0; h < NG; ++h) {
+          const uint4 x = ld_cg(mine + (G + par * NG + h) * slot_stride + i);
+          if (h == 0) acc_set(a, x); else acc_add(a, x);
+        }
+        const uint4 y = acc_pack(a);
+        st_plain(mine + (G + 2 * NG) * slot_stride + i, y);
+        st_plain(dst + gi, y);
+      }
+    }
+    ok = exchange(me, kFlagHierAG, c, seq, gpeers, ng, w, kStageAG);
+    if (!ok) break;
+    // 3. intra-group all-gather by loads
+    for (int i = threadIdx.x; i < chp; i += blockDim.x) {
+      for (int m = 0; m < G; ++m) {
+        if (m == l) continue;
+        const int64_t gi = tbase + static_cast<int64_t>(m) * chp + i;
+        if (gi < p.npacks)
+          st_plain(dst + gi, ld_cg(region(p.member[g][m]) + (G + 2 * NG) * slot_stride + i));
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) st_volatile_u32(&pad_of(me, rank)->hier_rounds[c], base_rounds + p.rounds);
+  end_call(me, epoch);
+}
+
+// ---------------------------------------------------------- oneshot pull ----
+template <typename T, int WS>
+__global__ void __launch_bounds__(kThreads) k_oneshot_pull(const __grid_constant__ ARParams p) {
+  const RankView& me = p.v[blockIdx.y];
+  const int rank = me.rank;
+  const uint32_t epoch = begin_call(me);
+  const WaitCtx w = make_wait(p, me, epoch);
+  const int64_t per = ceil_div<int64_t>(p.npacks, gridDim.x);
+  const int64_t beg = per * blockIdx.x;
+  const int64_t end = min(p.npacks, beg + per);
+  int peers[WS - 1];
+  all_peers<WS>(rank, peers);
+  const uint64_t seq = make_seq(epoch, 0);
+  bool ok = exchange(me, kFlagPullStart, blockIdx.x, seq, peers, WS - 1, w, kStagePullStart);
+  if (ok) {
+    const RankData rd = *me.reg;
+    uint4* dst = reinterpret_cast<uint4*>(me.out);
+    for (int64_t i = beg + threadIdx.x; i < end; i += blockDim.x) {
+      uint4 x[WS];
+#pragma unroll
+      for (int q = 0; q < WS; ++q) x[q] = ld_cg(reinterpret_cast<const uint4*>(rd.ptrs[q]) + i);
+      Acc<T> a;
+      acc_set(a, x[0]);
+#pragma unroll
+      for (int q = 1; q < WS; ++q) acc_add(a, x[q]);
+      st_plain(dst + i, acc_pack(a));
+    }
+    // nobody may overwrite its input while a peer still reads it
+    exchange(me, kFlagPullEnd, blockIdx.x, seq, peers, WS - 1, w, kStagePullEnd);
+  }
+  end_call(me, epoch);
+}
+
+// ---------------------------------------------------------- NVLS oneshot ----
+template <typename T, int WS>
+__global__ void __launch_bounds__(kThreads) k_nvls_oneshot(const __grid_constant__ ARParams p) {
+  const RankView& me = p.v[blockIdx.y];
+  const uint32_t epoch = begin_call(me);
+  const WaitCtx w = make_wait(p, me, epoch);
+  const int b = blockIdx.x;
+  const int parity = epoch & 1;
+  const int64_t per = ceil_div<int64_t>(p.npacks, gridDim.x);
+  const int64_t beg = per * b;
+  const int64_t end = min(p.npacks, beg + per);
+  const uint4* src = reinterpret_cast<const uint4*>(me.in);
+  uint4* dst = reinterpret_cast<uint4*>(me.out);
+  const int64_t off = p.L.mc_oneshot_off + parity * p.L.oneshot_max;
+  uint4* uc = reinterpret_cast<uint4*>(me.uc + off);
+  const uint4* mc = reinterpret_cast<const uint4*>(me.mc + off);
+  NvlsPad* upad = reinterpret_cast<NvlsPad*>(me.uc);
+  NvlsPad* mpad = reinterpret_cast<NvlsPad*>(me.mc);
+  for (int64_t i = beg + threadIdx.x; i < end; i += blockDim.x) st_plain(uc + i, ld_plain(src + i));
+  __syncthreads();
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) {
+    const uint32_t calls = upad->rounds[b][1] + 1u;
+    mm_red_add_release(&mpad->cnt[b][0][0], 1u);
+    s_ok = wait_geq_u32(&upad->cnt[b][0][0], calls * WS, w, kStageNvls1);
+    upad->rounds[b][1] = calls;
+  }
+  __syncthreads();
+  if (s_ok) {
+    for (int64_t i = beg + threadIdx.x; i < end; i += blockDim.x) st_plain(dst + i, mm_ld_reduce<T>(mc + i));
+  }
+  end_call(me, epoch);
+}
+
+// ---------------------------------------------------------- NVLS twoshot ----
+template <typename T, int WS>
+__global__ void __launch_bounds__(kThreads) k_nvls_twoshot(const __grid_constant__ ARParams p) {
+  const RankView& me = p.v[blockIdx.y];
+  const int rank = me.rank;
+  const uint32_t epoch = begin_call(me);
+  const WaitCtx w = make_wait(p, me, epoch);
+  const int c = blockIdx.x;
+  const int chp = p.chunk_packs;
+  const int64_t tile = static_cast<int64_t>(WS) * chp;
+  const int64_t stripe = tile * gridDim.x;
+  const int64_t slot_stride = p.L.chunk_max / 16;
+  const int64_t cta_off = p.L.mc_twoshot_off + static_cast<int64_t>(c) * WS * p.L.chunk_max;
+  uint4* uc = reinterpret_cast<uint4*>(me.uc + cta_off);
+  uint4* mc = reinterpret_cast<uint4*>(me.mc + cta_off);
+  NvlsPad* upad = reinterpret_cast<NvlsPad*>(me.uc);
+  NvlsPad* mpad = reinterpret_cast<NvlsPad*>(me.mc);
+  const uint4* src = reinterpret_cast<const uint4*>(me.in);
+  uint4* dst = reinterpret_cast<uint4*>(me.out);
+  __shared__ uint32_t s_base;
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) s_base = upad->rounds[c][0];
+  __syncthreads();
+  const uint32_t base = s_base;
+  bool ok = true;
+  for (int r = 0; r < p.rounds && ok; ++r) {
+    const int64_t tbase = r * stripe + c * tile;
+    const uint32_t target = (base + r + 1u) * WS;
+    // 1. copy the whole tile in (every chunk)
+    for (int j = 0; j < WS; ++j) {
+      for (int i = threadIdx.x; i < chp; i += blockDim.x) {
+        const int64_t g = tbase + static_cast<int64_t>(j) * chp + i;
+        if (g < p.npacks) st_plain(uc + j * slot_stride + i, ld_plain(src + g));
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      mm_red_add_release(&mpad->cnt[c][0][0], 1u);
+      s_ok = wait_geq_u32(&upad->cnt[c][0][0], target, w, kStageNvls1);
+    }
+    __syncthreads();
+    ok = s_ok;
+    if (!ok) break;
+    // 2. reduce my chunk in the switch and broadcast the result
+    for (int i = threadIdx.x; i < chp; i += blockDim.x) {
+      const int64_t g = tbase + static_cast<int64_t>(rank) * chp + i;
+      if (g < p.npacks) {
+        const uint4 y = mm_ld_reduce<T>(mc + rank * slot_stride + i);
+        mm_st<T>(mc + rank * slot_stride + i, y);
+        st_plain(dst + g, y);
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      mm_red_add_release(&mpad->cnt[c][1][0], 1u);
+      s_ok = wait_geq_u32(&upad->cnt[c][1][0], target, w, kStageNvls2);
+    }
+    __syncthreads();
+    ok = s_ok;
+    if (!ok) break;
+    // 3. copy the other owners' results out of my local copy
+    for (int j = 0; j < WS; ++j) {
+      if (j == rank) continue;
+      for (int i = threadIdx.x; i < chp; i += blockDim.x) {
+        const int64_t g = tbase + static_cast<int64_t>(j) * chp + i;
+        if (g < p.npacks) st_plain(dst + g, ld_cg(uc + j * slot_stride + i));
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) upad->rounds[c][0] = base + p.rounds;
+  end_call(me, epoch);
+}
+
+template <typename T, int WS>
+cudaError_t launch_ws(int algo, const ARParams& p, dim3 grid, cudaStream_t s, bool coop) {
+  void* fn = nullptr;
+  switch (algo) {
+    case kAlgoOneshot: fn = reinterpret_cast<void*>(&k_oneshot<T, WS>); break;
+    case kAlgoTwoshot: fn = reinterpret_cast<void*>(&k_twoshot<T, WS>); break;
+    case kAlgoHier: fn = reinterpret_cast<void*>(&k_hier<T>); break;
+    case kAlgoOneshotPull: fn = reinterpret_cast<void*>(&k_oneshot_pull<T, WS>); break;
+    case kAlgoNvlsOneshot: fn = reinterpret_cast<void*>(&k_nvls_oneshot<T, WS>); break;
+    case kAlgoNvlsTwoshot: fn = reinterpret_cast<void*>(&k_nvls_twoshot<T, WS>); break;
+    default: return cudaErrorInvalidValue;
+  }
+  void* args[] = {const_cast<ARParams*>(&p)};
+  if (coop) return cudaLaunchCooperativeKernel(fn, grid, dim3(kThreads), args, 0, s);
+  return cudaLaunchKernel(fn, grid, dim3(kThreads), args, 0, s);
+}
+
+template <typename T>
+cudaError_t launch_t(int algo, const ARParams& p, dim3 grid, cudaStream_t s, bool coop) {
+  switch (p.ws) {
+    case 2: return launch_ws<T, 2>(algo, p, grid, s, coop);
+    case 3: return launch_ws<T, 3>(algo, p, grid, s, coop);
+    case 4: return launch_ws<T, 4>(algo, p, grid, s, coop);
+    case 5: return launch_ws<T, 5>(algo, p, grid, s, coop);
+    case 6: return launch_ws<T, 6>(algo, p, grid, s, coop);
+    case 7: return launch_ws<T, 7>(algo, p, grid, s, coop);
+    case 8: return launch_ws<T, 8>(algo, p, grid, s, coop);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace
+
+int allreduce_threads() { return kThreads; }
+
+cudaError_t launch_allreduce(int algo, int dtype, const ARParams& p, dim3 grid, cudaStream_t s,
+                             bool cooperative) {
+  if (algo == kAlgoCopy) {
+    void* args[] = {const_cast<ARParams*>(&p)};
+    void* fn = reinterpret_cast<void*>(&k_copy);
+    if (cooperative) return cudaLaunchCooperativeKernel(fn, grid, dim3(kThreads), args, 0, s);
+    return cudaLaunchKernel(fn, grid, dim3(kThreads), args, 0, s);
+  }
+  switch (dtype) {
+    case kF32: return launch_t<float>(algo, p, grid, s, cooperative);
+    case kF16: return launch_t<__half>(algo, p, grid, s, cooperative);
+    case kBF16: return launch_t<__nv_bfloat16>(algo, p, grid, s, cooperative);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace nab

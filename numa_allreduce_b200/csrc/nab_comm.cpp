@@ -1,0 +1,420 @@
+// Host runtime of the allreduce library. See nab_comm.h.
+#include "nab_comm.h"
+
+#include <algorithm>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+
+#include "nab_driver.h"
+#include "nab_kernels.h"
+
+namespace nab {
+
+namespace {
+
+constexpr int64_t kAlign = 4096;
+
+int64_t round_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
+
+int64_t ceil_div_host(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+template <typename T>
+T clampv(T v, T lo, T hi) {
+  return std::max(lo, std::min(v, hi));
+}
+
+}  // namespace
+
+std::string cuda_error_string(cudaError_t e) { return cudaGetErrorString(e); }
+
+void* driver_entry(const char* name) {
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  cudaError_t e = cudaGetDriverEntryPointByVersion(name, &fn, 12000, cudaEnableDefault, &q);
+  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr)
+    throw std::runtime_error(std::string("CUDA driver entry point unavailable: ") + name);
+  return fn;
+}
+
+std::string cu_error_string(CUresult r) {
+  using Fn = CUresult (*)(CUresult, const char**);
+  const char* s = nullptr;
+  try {
+    driver_fn<Fn>("cuGetErrorString")(r, &s);
+  } catch (...) {
+  }
+  return s ? std::string(s) : ("CUresult " + std::to_string(static_cast<int>(r)));
+}
+
+Layout make_layout(int ws, const CommConfig& cfg) {
+  if (ws < 1 || ws > kMaxRanks) throw std::invalid_argument("world size must be in [1, 8]");
+  if (cfg.max_ctas < 1 || cfg.max_ctas > kMaxBlocks || cfg.oneshot_ctas < 1 ||
+      cfg.oneshot_ctas > kMaxBlocks)
+    throw std::invalid_argument("CTA counts must be in [1, 160]");
+  if (cfg.chunk_max < 16 * 512 || cfg.chunk_max % 16 != 0)
+    throw std::invalid_argument("chunk_max must be a multiple of 16 and >= 8 KiB");
+  if (cfg.oneshot_max % 16 != 0) throw std::invalid_argument("oneshot_max must be a multiple of 16");
+  Layout L{};
+  int64_t off = round_up(static_cast<int64_t>(sizeof(SignalPad)), kAlign);
+  L.oneshot_off = off;
+  L.oneshot_max = cfg.oneshot_max;
+  off += round_up(2 * ws * cfg.oneshot_max, kAlign);
+  L.chunk_max = cfg.chunk_max;
+  L.max_ctas = cfg.max_ctas;
+  L.twoshot_off = off;
+  off += round_up(static_cast<int64_t>(cfg.max_ctas) * (ws + 1) * cfg.chunk_max, kAlign);
+  L.hier_off = off;
+  off += round_up(static_cast<int64_t>(cfg.max_ctas) * (2 * ws + 2) * cfg.chunk_max, kAlign);
+  L.fused_off = off;
+  L.fused_bytes = round_up(cfg.fused_bytes, kAlign);
+  off += 2 * ws * L.fused_bytes;
+  L.fused2_off = off;
+  off += static_cast<int64_t>(cfg.max_ctas) * (ws + 1) * kFusedMaxHidden * 2;
+  L.ws_bytes = off;
+  int64_t moff = round_up(static_cast<int64_t>(sizeof(NvlsPad)), kAlign);
+  L.mc_oneshot_off = moff;
+  moff += round_up(2 * cfg.oneshot_max, kAlign);
+  L.mc_twoshot_off = moff;
+  moff += round_up(static_cast<int64_t>(cfg.max_ctas) * ws * cfg.chunk_max, kAlign);
+  L.mc_bytes = moff;
+  return L;
+}
+
+Communicator::Communicator(int rank, int ws, const std::vector<char*>& wsp, void* rank_data,
+                           size_t rank_data_bytes, const CommConfig& cfg, bool full_nvlink)
+    : rank_(rank), ws_(ws), cfg_(cfg), L_(make_layout(ws, cfg)), full_nvlink_(full_nvlink),
+      wsp_(wsp) {
+  if (rank < 0 || rank >= ws) throw std::invalid_argument("rank out of range");
+  if (static_cast<int>(wsp.size()) != ws)
+    throw std::invalid_argument("need one workspace pointer per rank");
+  for (auto* p : wsp)
+    if (p == nullptr || reinterpret_cast<uintptr_t>(p) % 256 != 0)
+      throw std::invalid_argument("workspace pointers must be non-null and 256-byte aligned");
+  NAB_CUDA_CHECK(cudaGetDevice(&device_));
+  rd_base_ = rd_cur_ = reinterpret_cast<RankData*>(rank_data);
+  rd_end_ = rd_base_ + (rank_data ? rank_data_bytes / sizeof(RankData) : 0);
+  NAB_CUDA_CHECK(cudaMalloc(&err_dev_, sizeof(ErrorState)));
+  NAB_CUDA_CHECK(cudaMemset(err_dev_, 0, sizeof(ErrorState)));
+  NAB_CUDA_CHECK(cudaHostAlloc(&err_host_, 64, cudaHostAllocMapped | cudaHostAllocPortable));
+  std::memset(err_host_, 0, 64);
+}
+
+Communicator::~Communicator() {
+  for (auto& kv : opened_) cudaIpcCloseMemHandle(kv.second);
+  if (err_dev_) cudaFree(err_dev_);
+  if (err_host_) cudaFreeHost(err_host_);
+}
+
+void Communicator::set_groups(const std::vector<std::vector<int>>& groups) {
+  const int ng = static_cast<int>(groups.size());
+  if (ng < 1 || ng > ws_) throw std::invalid_argument("bad number of groups");
+  const int gs = static_cast<int>(groups[0].size());
+  if (gs * ng != ws_) throw std::invalid_argument("groups must partition the ranks equally");
+  std::vector<int> seen(ws_, 0);
+  for (int g = 0; g < ng; ++g) {
+    if (static_cast<int>(groups[g].size()) != gs)
+      throw std::invalid_argument("all groups must have the same size");
+    for (int l = 0; l < gs; ++l) {
+      const int r = groups[g][l];
+      if (r < 0 || r >= ws_ || seen[r]++) throw std::invalid_argument("groups must partition ranks");
+      group_of_[r] = static_cast<int8_t>(g);
+      lidx_of_[r] = static_cast<int8_t>(l);
+      member_[g][l] = static_cast<int8_t>(r);
+    }
+  }
+  ngroups_ = ng;
+  gsize_ = gs;
+}
+
+void Communicator::attach_nvls(char* mc, char* uc, int64_t bytes) {
+  if (bytes < L_.mc_bytes) throw std::invalid_argument("NVLS workspace too small");
+  mc_ = mc;
+  uc_ = uc;
+  mc_bytes_ = bytes;
+}
+
+RankData* Communicator::reserve_rank_data() {
+  if (rd_cur_ >= rd_end_) throw std::runtime_error("RankData registry is full");
+  return rd_cur_++;
+}
+
+void Communicator::register_buffer(const std::vector<void*>& ptrs) {
+  if (static_cast<int>(ptrs.size()) != ws_) throw std::invalid_argument("need one pointer per rank");
+  RankData rd{};
+  for (int i = 0; i < ws_; ++i) rd.ptrs[i] = ptrs[i];
+  RankData* slot = reserve_rank_data();
+  NAB_CUDA_CHECK(cudaMemcpy(slot, &rd, sizeof(rd), cudaMemcpyHostToDevice));
+  buffers_[ptrs[rank_]] = slot;
+}
+
+std::pair<std::string, std::vector<int64_t>> Communicator::graph_buffer_ipc_meta() {
+  using GetAttr = CUresult (*)(void*, CUpointer_attribute, CUdeviceptr);
+  auto get_attr = driver_fn<GetAttr>("cuPointerGetAttribute");
+  std::string handles;
+  handles.reserve(graph_unreg_.size() * sizeof(cudaIpcMemHandle_t));
+  std::vector<int64_t> offsets;
+  offsets.reserve(graph_unreg_.size());
+  for (const void* ptr : graph_unreg_) {
+    CUdeviceptr base = 0;
+    NAB_CU_CHECK(get_attr(&base, CU_POINTER_ATTRIBUTE_RANGE_START_ADDR,
+                          reinterpret_cast<CUdeviceptr>(ptr)));
+    cudaIpcMemHandle_t h;
+    NAB_CUDA_CHECK(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)));
+    handles.append(reinterpret_cast<const char*>(&h), sizeof(h));
+    offsets.push_back(reinterpret_cast<const char*>(ptr) - reinterpret_cast<const char*>(base));
+  }
+  return {handles, offsets};
+}
+
+void Communicator::register_graph_buffers(const std::vector<std::string>& handles,
+                                          const std::vector<std::vector<int64_t>>& offsets) {
+  const size_t n = graph_unreg_.size();
+  if (static_cast<int>(handles.size()) != ws_ || static_cast<int>(offsets.size()) != ws_)
+    throw std::invalid_argument("need handles and offsets from every rank");
+  std::vector<RankData> rds(n);
+  for (int j = 0; j < ws_; ++j) {
+    if (handles[j].size() != n * sizeof(cudaIpcMemHandle_t) || offsets[j].size() != n)
+      throw std::invalid_argument("ranks captured different numbers of buffers");
+    for (size_t i = 0; i < n; ++i) {
+      if (j == rank_) {
+        rds[i].ptrs[j] = graph_unreg_[i];
+        continue;
+      }
+      const std::string h = handles[j].substr(i * sizeof(cudaIpcMemHandle_t), sizeof(cudaIpcMemHandle_t));
+      auto it = opened_.find(h);
+      char* base;
+      if (it == opened_.end()) {
+        base = static_cast<char*>(ipc_open(h));
+        opened_[h] = base;
+      } else {
+        base = it->second;
+      }
+      rds[i].ptrs[j] = base + offsets[j][i];
+    }
+  }
+  for (size_t i = 0; i < n; ++i)
+    NAB_CUDA_CHECK(cudaMemcpy(buffers_.at(graph_unreg_[i]), &rds[i], sizeof(RankData),
+                              cudaMemcpyHostToDevice));
+  graph_unreg_.clear();
+}
+
+LaunchPlan Communicator::plan(int64_t nbytes, int algo, bool registered) const {
+  LaunchPlan pl;
+  const int64_t npacks = nbytes / 16;
+  if (ws_ == 1) {
+    pl.algo = kAlgoCopy;
+    pl.grid = dim3(static_cast<unsigned>(clampv<int64_t>(ceil_div_host(npacks, 4 * 512), 1, 148 * 4)));
+    return pl;
+  }
+  if (algo == kAlgoAuto) {
+    if (registered && nbytes <= cfg_.oneshot_max && nbytes <= (64 << 10))
+      algo = kAlgoOneshotPull;
+    else if (nbytes <= std::min<int64_t>(cfg_.oneshot_max, 256 << 10))
+      algo = kAlgoOneshot;
+    else if (mc_ != nullptr)
+      algo = kAlgoNvlsTwoshot;
+    else
+      algo = kAlgoTwoshot;
+  }
+  pl.algo = algo;
+  switch (algo) {
+    case kAlgoOneshot:
+    case kAlgoNvlsOneshot:
+    case kAlgoOneshotPull: {
+      if (algo != kAlgoOneshotPull && nbytes > cfg_.oneshot_max)
+        throw std::invalid_argument("message exceeds the one-shot workspace");
+      const int64_t b = clampv<int64_t>(ceil_div_host(npacks, 1024), 1, cfg_.oneshot_ctas);
+      pl.grid = dim3(static_cast<unsigned>(b));
+      break;
+    }
+    case kAlgoTwoshot:
+    case kAlgoNvlsTwoshot:
+    case kAlgoHier: {
+      const int parts = (algo == kAlgoHier) ? gsize_ : ws_;
+      const int64_t chunk_cap = L_.chunk_max / 16;
+      const int64_t C = clampv<int64_t>(ceil_div_host(npacks, static_cast<int64_t>(parts) * 512), 1,
+                                        cfg_.max_ctas);
+      const int64_t chp = std::min(chunk_cap, std::max<int64_t>(1, ceil_div_host(npacks, C * parts)));
+      const int64_t rounds = ceil_div_host(npacks, C * parts * chp);
+      if (rounds >= (int64_t(1) << kSeqShift)) throw std::invalid_argument("message too large");
+      pl.grid = dim3(static_cast<unsigned>(C));
+      pl.chunk_packs = static_cast<int>(chp);
+      pl.rounds = static_cast<int>(rounds);
+      break;
+    }
+    default:
+      throw std::invalid_argument("unknown allreduce algorithm " + std::to_string(algo));
+  }
+  if ((algo == kAlgoNvlsOneshot || algo == kAlgoNvlsTwoshot) && mc_ == nullptr)
+    throw std::invalid_argument("NVLS protocol requested but no multicast workspace attached");
+  if (algo == kAlgoHier && ngroups_ == 0)
+    throw std::invalid_argument("hierarchical protocol requested but no groups set");
+  return pl;
+}
+
+RankView Communicator::view(const void* in, void* out, const RankData* reg) const {
+  RankView v{};
+  v.in = static_cast<const char*>(in);
+  v.out = static_cast<char*>(out);
+  for (int i = 0; i < ws_; ++i) v.wsp[i] = wsp_[i];
+  v.reg = reg;
+  v.mc = mc_;
+  v.uc = uc_;
+  v.rank = rank_;
+  return v;
+}
+
+void Communicator::fill_params(ARParams& p, const LaunchPlan& pl, int64_t nbytes) const {
+  p.err = err_dev_;
+  p.err_host = err_host_;
+  p.npacks = nbytes / 16;
+  p.timeout_ns = cfg_.timeout_ns;
+  p.ws = ws_;
+  p.chunk_packs = pl.chunk_packs;
+  p.rounds = pl.rounds;
+  p.ngroups = ngroups_;
+  p.gsize = gsize_;
+  std::memcpy(p.group_of, group_of_, sizeof(group_of_));
+  std::memcpy(p.lidx_of, lidx_of_, sizeof(lidx_of_));
+  std::memcpy(p.member, member_, sizeof(member_));
+  p.L = L_;
+}
+
+int Communicator::allreduce(cudaStream_t s, const void* in, void* out, int64_t nbytes, int dtype,
+                            int algo, bool registered) {
+  if (nbytes <= 0 || nbytes % 16 != 0)
+    throw std::invalid_argument("allreduce size must be a positive multiple of 16 bytes");
+  if (dtype != kF32 && dtype != kF16 && dtype != kBF16)
+    throw std::invalid_argument("allreduce supports float32, float16 and bfloat16");
+  if (reinterpret_cast<uintptr_t>(in) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
+    throw std::invalid_argument("allreduce buffers must be 16-byte aligned");
+  if (ws_ == 1 && in == out) return kAlgoCopy;  // nothing to do
+  const LaunchPlan pl = plan(nbytes, algo, registered);
+  const RankData* reg = nullptr;
+  if (pl.algo == kAlgoOneshotPull) {
+    auto it = buffers_.find(in);
+    if (it != buffers_.end()) {
+      reg = it->second;
+    } else {
+      cudaStreamCaptureStatus st;
+      NAB_CUDA_CHECK(cudaStreamIsCapturing(s, &st));
+      if (st != cudaStreamCaptureStatusActive)
+        throw std::invalid_argument("pull protocol needs a registered input buffer");
+      RankData* slot = reserve_rank_data();
+      buffers_[in] = slot;
+      graph_unreg_.push_back(in);
+      reg = slot;
+    }
+  }
+  ARParams p{};
+  fill_params(p, pl, nbytes);
+  p.v[0] = view(in, out, reg);
+  const cudaError_t e = launch_allreduce(pl.algo, dtype, p, pl.grid, s, false);
+  if (e != cudaSuccess)
+    throw std::runtime_error(std::string("allreduce launch failed: ") + cudaGetErrorString(e));
+  count_launch();
+  return pl.algo;
+}
+
+uint32_t Communicator::error_code() const {
+  return *reinterpret_cast<volatile uint32_t*>(err_host_);
+}
+
+ErrorState Communicator::error_state() const {
+  ErrorState st{};
+  NAB_CUDA_CHECK(cudaMemcpy(&st, err_dev_, sizeof(st), cudaMemcpyDeviceToHost));
+  return st;
+}
+
+void Communicator::reset() {
+  NAB_CUDA_CHECK(cudaDeviceSynchronize());
+  NAB_CUDA_CHECK(cudaMemset(wsp_[rank_], 0, sizeof(SignalPad)));
+  if (uc_) NAB_CUDA_CHECK(cudaMemset(uc_, 0, sizeof(NvlsPad)));
+  NAB_CUDA_CHECK(cudaMemset(err_dev_, 0, sizeof(ErrorState)));
+  NAB_CUDA_CHECK(cudaDeviceSynchronize());
+  std::memset(err_host_, 0, 64);
+}
+
+int emulate_allreduce(const std::vector<Communicator*>& comms, cudaStream_t s,
+                      const std::vector<const void*>& ins, const std::vector<void*>& outs,
+                      int64_t nbytes, int dtype, int algo, int participants) {
+  const int ws = static_cast<int>(comms.size());
+  if (participants < 0) participants = ws;
+  if (participants < 1 || participants > ws) throw std::invalid_argument("bad participant count");
+  if (ws < 2 || ws > kMaxRanks || static_cast<int>(ins.size()) != ws ||
+      static_cast<int>(outs.size()) != ws)
+    throw std::invalid_argument("emulation needs 2..8 communicators and one buffer per rank");
+  if (nbytes <= 0 || nbytes % 16 != 0)
+    throw std::invalid_argument("allreduce size must be a positive multiple of 16 bytes");
+  if (algo == kAlgoNvlsOneshot || algo == kAlgoNvlsTwoshot || algo == kAlgoOneshotPull)
+    throw std::invalid_argument("NVLS and pull protocols cannot be emulated on one GPU");
+  Communicator* c0 = comms[0];
+  LaunchPlan pl = c0->plan(nbytes, algo, false);
+  // Every CTA of every emulated rank must be resident at once: cap the grid
+  // at one 512-thread CTA per SM and re-plan the tiling for that grid.
+  int dev = 0, sms = 0;
+  NAB_CUDA_CHECK(cudaGetDevice(&dev));
+  NAB_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int64_t cap = std::max(1, sms / ws);
+  if (pl.grid.x > cap) {
+    const int64_t npacks = nbytes / 16;
+    pl.grid.x = static_cast<unsigned>(cap);
+    if (pl.rounds > 0) {
+      ARParams tmp{};
+      c0->fill_params(tmp, pl, nbytes);
+      const int parts = (pl.algo == kAlgoHier) ? tmp.gsize : ws;
+      const int64_t chunk_cap = c0->layout().chunk_max / 16;
+      const int64_t chp = std::min(chunk_cap, std::max<int64_t>(1, ceil_div_host(npacks, cap * parts)));
+      pl.chunk_packs = static_cast<int>(chp);
+      pl.rounds = static_cast<int>(ceil_div_host(npacks, cap * parts * chp));
+    }
+  }
+  ARParams p{};
+  c0->fill_params(p, pl, nbytes);
+  for (int r = 0; r < ws; ++r) {
+    if (comms[r]->rank() != r) throw std::invalid_argument("communicators must be in rank order");
+    p.v[r] = comms[r]->view(ins[r], outs[r], nullptr);
+  }
+  pl.grid.y = participants;
+  const cudaError_t e = launch_allreduce(pl.algo, dtype, p, pl.grid, s, true);
+  if (e != cudaSuccess)
+    throw std::runtime_error(std::string("emulated allreduce launch failed: ") + cudaGetErrorString(e));
+  for (int r = 0; r < participants; ++r) comms[r]->count_launch();
+  return pl.algo;
+}
+
+void* ipc_alloc_shared(size_t bytes, cudaStream_t s, std::string* handle_out) {
+  void* buf = nullptr;
+  cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+  NAB_CUDA_CHECK(cudaThreadExchangeStreamCaptureMode(&mode));
+  cudaError_t e = cudaMalloc(&buf, bytes);
+  if (e == cudaSuccess) e = cudaMemsetAsync(buf, 0, bytes, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  cudaThreadExchangeStreamCaptureMode(&mode);
+  if (e != cudaSuccess) {
+    if (buf) cudaFree(buf);
+    throw std::runtime_error(std::string("shared buffer allocation failed: ") + cudaGetErrorString(e));
+  }
+  if (handle_out) {
+    cudaIpcMemHandle_t h;
+    NAB_CUDA_CHECK(cudaIpcGetMemHandle(&h, buf));
+    handle_out->assign(reinterpret_cast<const char*>(&h), sizeof(h));
+  }
+  return buf;
+}
+
+void* ipc_open(const std::string& handle) {
+  if (handle.size() != sizeof(cudaIpcMemHandle_t)) throw std::invalid_argument("bad IPC handle size");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle.data(), sizeof(h));
+  void* p = nullptr;
+  NAB_CUDA_CHECK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  return p;
+}
+
+void ipc_close(void* ptr) { NAB_CUDA_CHECK(cudaIpcCloseMemHandle(ptr)); }
+
+void ipc_free(void* ptr) { NAB_CUDA_CHECK(cudaFree(ptr)); }
+
+}  // namespace nab

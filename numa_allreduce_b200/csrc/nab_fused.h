@@ -1,0 +1,41 @@
+// Fused tensor-parallel layer tail: allreduce of the row-parallel partial
+// output, residual add and RMSNorm in one kernel (bf16).
+//
+//   z        = sum over ranks of inp  (fp32, rank order) + residual
+//   residual = bf16(z)
+//   out      = bf16(residual * rsqrt(mean(residual^2) + eps) * weight)
+//
+// No counterpart in the reference (it has no fused ops); this is the B200
+// build's TP-layer path. The norm is computed from the bf16 residual, as an
+// unfused "allreduce, then add, then RMSNorm" sequence would, so every rank
+// can recompute it from gathered residual rows and all ranks agree bit for bit.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <vector>
+
+#include "nab_comm.h"
+
+namespace nab {
+
+enum FusedAlgo : int { kFusedAuto = 0, kFusedOneshot = 1, kFusedTwoshot = 2 };
+
+// Returns the protocol used.
+int fused_allreduce_rmsnorm(Communicator& c, cudaStream_t s, const void* inp, void* residual,
+                            const void* weight, void* out, int64_t T, int64_t H, float eps, int algo);
+
+// Single-GPU emulation of the fused op over ws ranks (cooperative launch).
+int emulate_fused_allreduce_rmsnorm(const std::vector<Communicator*>& comms, cudaStream_t s,
+                                    const std::vector<const void*>& ins,
+                                    const std::vector<void*>& residuals,
+                                    const std::vector<const void*>& weights,
+                                    const std::vector<void*>& outs, int64_t T, int64_t H, float eps,
+                                    int algo);
+
+// Local residual add + RMSNorm (no communication): the world-size-1 path and
+// the norm of the unfused baseline.
+void rmsnorm_residual(cudaStream_t s, const void* inp, void* residual, const void* weight, void* out,
+                      int64_t T, int64_t H, float eps);
+
+}  // namespace nab

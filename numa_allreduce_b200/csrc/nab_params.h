@@ -1,0 +1,63 @@
+// Kernel parameter block shared by the host runtime and the device kernels.
+//
+// One RankView describes everything a rank needs. A real multi-process launch
+// fills v[0] and uses gridDim.y == 1. A single-GPU emulation launch fills
+// v[0..ws) with one view per emulated rank (all buffers on the same GPU) and
+// uses gridDim.y == ws with a cooperative launch, so the CTAs of different
+// emulated ranks that wait on each other are guaranteed to be co-resident.
+#pragma once
+
+#include <cstdint>
+
+#include "nab_common.h"
+
+namespace nab {
+
+struct RankView {
+  const char* in;
+  char* out;
+  char* wsp[kMaxRanks];  // IPC workspace base of every rank, as mapped here
+  const RankData* reg;   // peers' registered input pointers (pull protocol)
+  char* mc;              // multicast address of the NVLS workspace (or null)
+  char* uc;              // this rank's own unicast view of the NVLS workspace
+  int rank;
+  int pad_;
+};
+
+// Byte offsets inside the IPC workspace (ws_*) and the NVLS workspace (mc_*).
+struct Layout {
+  int64_t oneshot_off;    // [2 parities][ws slots][oneshot_max]
+  int64_t oneshot_max;    // bytes per slot
+  int64_t twoshot_off;    // [cta][ws rs slots + 1 result][chunk_max]
+  int64_t hier_off;       // [cta][gsize rs + 2*ngroups x + 1 result][chunk_max]
+  int64_t fused_off;      // fused one-shot: [2 parities][ws slots][fused_bytes]
+  int64_t fused_bytes;    // bytes per fused one-shot slot
+  int64_t fused2_off;     // fused two-shot: [cta][ws rs rows + 1 result row][kFusedMaxHidden*2]
+  int64_t chunk_max;      // bytes per owner chunk per round (tiled protocols)
+  int64_t ws_bytes;       // total IPC workspace bytes
+  int64_t mc_oneshot_off; // [2 parities][oneshot_max]
+  int64_t mc_twoshot_off; // [cta][ws chunks][chunk_max]
+  int64_t mc_bytes;
+  int max_ctas;           // CTA slots the workspace was sized for
+  int pad_;
+};
+
+struct ARParams {
+  RankView v[kMaxRanks];
+  ErrorState* err;
+  uint32_t* err_host;
+  int64_t npacks;        // message size in 16-byte packs
+  uint64_t timeout_ns;
+  int ws;
+  int chunk_packs;       // packs per owner chunk per round
+  int rounds;            // rounds per CTA
+  int ngroups;           // hierarchical: number of groups
+  int gsize;             // hierarchical: ranks per group
+  int pad_;
+  int8_t group_of[kMaxRanks];
+  int8_t lidx_of[kMaxRanks];
+  int8_t member[kMaxRanks][kMaxRanks];  // [group][local index] -> rank
+  Layout L;
+};
+
+}  // namespace nab

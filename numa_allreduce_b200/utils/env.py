@@ -1,0 +1,101 @@
+"""Environment-variable configuration.
+
+Capability parity: the reference reads ``CUDA_VISIBLE_DEVICES`` and
+``VLLM_SKIP_P2P_CHECK`` through ``vllm.envs`` (src/numa_all_reduce.py:155,241)
+and documents ``VLLM_NUMA_AR_ENABLE``/``VLLM_NUMA_AR_DEBUG`` that the code never
+reads. Every variable below is actually read:
+
+=========================  ===================================================
+``NAB_DISABLE``            ``1`` disables the custom path (callers fall back)
+``NAB_ALGO``               force one protocol: ``oneshot``, ``twoshot``,
+                           ``nvls_oneshot``, ``nvls_twoshot``, ``hier``,
+                           ``pull``, ``nccl`` or ``auto`` (default)
+``NAB_MAX_SIZE``           largest message (bytes) the custom path takes
+``NAB_TIMEOUT_NS``         bound of every device-side wait (default 5 s)
+``NAB_TUNING_FILE``        JSON table of protocol thresholds (see select.py)
+``NAB_LOG_LEVEL``          logging level name (default WARNING)
+``NAB_NVLS``               ``0`` turns off NVLink SHARP (multicast) protocols
+``NAB_HIER_GROUPS``        explicit groups, e.g. ``0,1,2,3|4,5,6,7``
+``NAB_SKIP_P2P_CHECK``     ``1`` trusts the driver for peer access
+``NAB_CHECK``              ``1`` checks the device error word after every call
+``NAB_NVTX``               ``1`` wraps calls in NVTX ranges
+=========================  ===================================================
+"""
+
+from __future__ import annotations
+
+import os
+from dataclasses import dataclass, field
+
+ALGO_IDS = {
+    "auto": 0,
+    "oneshot": 1,
+    "twoshot": 2,
+    "nvls_oneshot": 3,
+    "nvls_twoshot": 4,
+    "hier": 5,
+    "pull": 6,
+    "copy": 7,
+}
+ALGO_NAMES = {v: k for k, v in ALGO_IDS.items()}
+NCCL = "nccl"
+
+
+def _flag(name: str, default: bool = False) -> bool:
+    v = os.environ.get(name)
+    if v is None:
+        return default
+    return v.strip().lower() in ("1", "true", "yes", "on")
+
+
+def _int(name: str, default: int | None) -> int | None:
+    v = os.environ.get(name)
+    if v is None or v.strip() == "":
+        return default
+    return int(v, 0)
+
+
+def parse_groups(spec: str) -> list[list[int]]:
+    """``"0,1,2,3|4,5,6,7"`` -> ``[[0, 1, 2, 3], [4, 5, 6, 7]]``."""
+    groups = []
+    for part in spec.split("|"):
+        part = part.strip()
+        if part:
+            groups.append([int(x) for x in part.split(",") if x.strip() != ""])
+    return groups
+
+
+@dataclass
+class EnvConfig:
+    disable: bool = False
+    algo: str = "auto"
+    max_size: int | None = None
+    timeout_ns: int = 5_000_000_000
+    tuning_file: str | None = None
+    log_level: str = "WARNING"
+    nvls: bool = True
+    hier_groups: list[list[int]] | None = None
+    skip_p2p_check: bool = False
+    check: bool = False
+    nvtx: bool = False
+    extra: dict = field(default_factory=dict)
+
+
+def read_env() -> EnvConfig:
+    algo = os.environ.get("NAB_ALGO", "auto").strip().lower()
+    if algo not in ALGO_IDS and algo != NCCL:
+        raise ValueError(f"NAB_ALGO={algo!r} is not one of {sorted(ALGO_IDS) + [NCCL]}")
+    groups = os.environ.get("NAB_HIER_GROUPS")
+    return EnvConfig(
+        disable=_flag("NAB_DISABLE"),
+        algo=algo,
+        max_size=_int("NAB_MAX_SIZE", None),
+        timeout_ns=_int("NAB_TIMEOUT_NS", 5_000_000_000),
+        tuning_file=os.environ.get("NAB_TUNING_FILE"),
+        log_level=os.environ.get("NAB_LOG_LEVEL", "WARNING"),
+        nvls=_flag("NAB_NVLS", True),
+        hier_groups=parse_groups(groups) if groups else None,
+        skip_p2p_check=_flag("NAB_SKIP_P2P_CHECK"),
+        check=_flag("NAB_CHECK"),
+        nvtx=_flag("NAB_NVTX"),
+    )
