@@ -1,0 +1,210 @@
+#!/usr/bin/env python3
+"""Allreduce sweep: p50 latency and bus bandwidth per protocol, dtype and size.
+
+BASELINE configs 2 and 3: contiguous 1-D tensors of 4 KiB .. 256 MiB (powers
+of two), N(0,1) with seed = rank, every protocol of this library plus NCCL and
+the reference's custom allreduce (``--ref``), 200 timed iterations after 20
+warm-up. Launch with torch.distributed.run, one process per GPU::
+
+    python -m torch.distributed.run --nproc-per-node 8 bench/sweep.py --dtypes bf16 --ref
+
+Modes: ``eager`` times back-to-back launches with CUDA events around every call
+(p50 over calls, max over ranks); ``graph`` captures ``--graph-calls`` calls of
+this library's kernels in one CUDA graph and reports replay time per call, i.e.
+device time without host launch overhead. ``--write-table`` turns the eager
+results into the selector's JSON tuning table.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+from numa_allreduce_b200 import NumaAwareAllReduce  # noqa: E402
+from numa_allreduce_b200.parallel.select import build_table  # noqa: E402
+from numa_allreduce_b200.utils.timing import busbw_gbs  # noqa: E402
+
+DT = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}
+NAMES = {torch.bfloat16: "bfloat16", torch.float16: "float16", torch.float32: "float32"}
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--sizes", default=",".join(str(4096 << i) for i in range(17)))
+    p.add_argument("--dtypes", default="bf16")
+    p.add_argument("--algos", default="auto", help="comma list, 'all' or 'auto' (selector)")
+    p.add_argument("--iters", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--mode", choices=["eager", "graph", "both"], default="both")
+    p.add_argument("--graph-calls", type=int, default=20)
+    p.add_argument("--nccl", action="store_true", default=True)
+    p.add_argument("--no-nccl", dest="nccl", action="store_false")
+    p.add_argument("--ref", action="store_true", help="include the reference's custom allreduce")
+    p.add_argument("--out", default=None)
+    p.add_argument("--write-table", default=None)
+    p.add_argument("--max-oneshot", type=int, default=1 << 20)
+    p.add_argument("--hier-groups", default=None, help="e.g. 0,1,2,3|4,5,6,7")
+    return p.parse_args()
+
+
+def max_over_ranks(vals):
+    t = torch.tensor(vals, dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def time_eager(fn, iters, warmup):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    dist.barrier()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+    for a, b in ev:
+        a.record()
+        fn()
+        b.record()
+    torch.cuda.synchronize()
+    return statistics.median(a.elapsed_time(b) * 1e3 for a, b in ev)
+
+
+def time_graph(fn, calls, reps, warmup):
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(calls):
+            fn()
+    for _ in range(max(1, warmup // calls)):
+        g.replay()
+    torch.cuda.synchronize()
+    dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    us = a.elapsed_time(b) * 1e3 / (reps * calls)
+    del g
+    return us
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=300),
+                            device_id=torch.device("cuda", local))
+    groups = None
+    if args.hier_groups:
+        from numa_allreduce_b200.utils.env import parse_groups
+
+        groups = parse_groups(args.hier_groups)
+    ar = NumaAwareAllReduce(dist.group.WORLD, device=local, hier_groups=groups, oneshot_max=args.max_oneshot)
+    ref = None
+    if args.ref:
+        sys.path.insert(0, os.path.join(ROOT, "baseline"))
+        try:
+            from ref_arm import load_reference_class
+
+            gloo = dist.new_group(backend="gloo")
+            ref = load_reference_class()(group=gloo, device=local)
+            if ref.disabled:
+                ref = None
+        except Exception as e:
+            if rank == 0:
+                print(f"reference unavailable: {e}", flush=True)
+            ref = None
+    sizes = [int(v) for v in args.sizes.split(",")]
+    if args.algos == "all":
+        algos = ["oneshot", "twoshot"] + (["nvls_oneshot", "nvls_twoshot"] if ar.has_nvls else []) + \
+                (["hier"] if ar.hier_groups else [])
+    elif args.algos == "auto":
+        algos = ["auto"]
+    else:
+        algos = args.algos.split(",")
+    rows = []
+    for dname in args.dtypes.split(","):
+        dtype = DT[dname]
+        esize = torch.tensor([], dtype=dtype).element_size()
+        for size in sizes:
+            n = size // esize
+            g = torch.Generator(device="cuda").manual_seed(rank)
+            x = torch.randn(n, generator=g, device="cuda", dtype=torch.float32).to(dtype)
+            out = torch.empty_like(x)
+            expect = x.float()
+            dist.all_reduce(expect)
+            cands = []
+            for algo in algos:
+                name = ar.algo_for(size, dtype) if algo == "auto" else algo
+                if name in ("oneshot", "nvls_oneshot") and size > args.max_oneshot:
+                    continue
+                if name == "nccl":
+                    continue
+                cands.append((algo if algo != "auto" else f"auto:{name}",
+                              (lambda nm=name: ar.all_reduce(x, out=out, algo=nm)), True))
+            if args.nccl:
+                y = x.clone()
+                cands.append(("nccl", lambda: dist.all_reduce(y), False))
+            if ref is not None and ref.should_use_numa_ar(x):
+                cands.append(("ref_custom_ar", lambda: ref.custom_all_reduce(x), False))
+            for label, fn, ours in cands:
+                ok = True
+                if ours:
+                    fn()
+                    torch.cuda.synchronize()
+                    ar.check()
+                    tol = 1e-5 * world if dtype == torch.float32 else 2e-2 * world
+                    ok = bool(torch.allclose(out.float(), expect, rtol=1e-2, atol=tol))
+                flag = torch.tensor([1 if ok else 0], device="cuda")
+                dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+                modes = ["eager"] if not ours or args.mode == "eager" else (
+                    ["graph"] if args.mode == "graph" else ["eager", "graph"])
+                for mode in modes:
+                    if mode == "eager":
+                        us = time_eager(fn, args.iters, args.warmup)
+                    else:
+                        reps = max(1, args.iters // args.graph_calls)
+                        us = time_graph(fn, args.graph_calls, reps, args.warmup)
+                    us = max_over_ranks([us])[0]
+                    row = {"world_size": world, "dtype": NAMES[dtype], "bytes": size, "algo": label,
+                           "mode": mode, "p50_us": round(us, 2), "busbw_gbs": round(busbw_gbs(size, us / 1e6, world), 1),
+                           "nvls": ar.has_nvls, "correct": bool(flag.item())}
+                    rows.append(row)
+                    if rank == 0:
+                        print(f"{NAMES[dtype]:>8} {size:>11} {label:>22} {mode:>5} {us:10.2f} us "
+                              f"{row['busbw_gbs']:8.1f} GB/s {'ok' if row['correct'] else 'WRONG'}", flush=True)
+    if rank == 0:
+        if args.out:
+            with open(args.out, "w") as f:
+                json.dump({"world_size": world, "nvls": ar.has_nvls, "rows": rows}, f, indent=1)
+        if args.write_table:
+            tab_rows = [dict(r, algo=r["algo"].split(":")[-1]) for r in rows
+                        if r["mode"] == "eager" and r["correct"] and not r["algo"].startswith("ref")]
+            with open(args.write_table, "w") as f:
+                json.dump(build_table(tab_rows), f, indent=1)
+    torch.cuda.synchronize()
+    ar.close()
+    if ref is not None:
+        ref.close()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

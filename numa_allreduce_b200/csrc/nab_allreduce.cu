@@ -73,9 +73,20 @@ __global__ void __launch_bounds__(kThreads) k_copy(const __grid_constant__ ARPar
   for (; i < p.npacks; i += stride) st_plain(dst + i, ld_plain(src + i));
 }
 
+// Loads in flight per thread: each phase issues all of its loads for U
+// consecutive packs before the first store, so a warp keeps ~8 independent
+// 16-byte requests outstanding (NVLink round trips are ~1-2 us).
+template <int WS>
+struct Unroll {
+  static constexpr int kPeer = (WS - 1) >= 8 ? 1 : 8 / (WS - 1);  // one load per peer per pack
+  static constexpr int kRed = WS >= 8 ? 1 : 8 / WS;               // WS loads per pack
+};
+
 // --------------------------------------------------------------- oneshot ----
 template <typename T, int WS>
-__global__ void __launch_bounds__(kThreads) k_oneshot(const __grid_constant__ ARParams p) {
+__global__ void __launch_bounds__(kThreads, 2) k_oneshot(const __grid_constant__ ARParams p) {
+  constexpr int U = 4;
+  constexpr int UR = Unroll<WS>::kRed;
   const RankView& me = p.v[blockIdx.y];
   const int rank = me.rank;
   const uint32_t epoch = begin_call(me);
@@ -91,10 +102,21 @@ __global__ void __launch_bounds__(kThreads) k_oneshot(const __grid_constant__ AR
            (static_cast<int64_t>(parity) * WS + src_rank) * slot_packs;
   };
   // 1. push my input into slot [rank] of every peer
-  for (int64_t i = beg + threadIdx.x; i < end; i += blockDim.x) {
-    const uint4 x = ld_plain(src + i);
+  for (int64_t i0 = beg + threadIdx.x; i0 < end; i0 += static_cast<int64_t>(blockDim.x) * U) {
+    uint4 x[U];
 #pragma unroll
-    for (int k = 1; k < WS; ++k) st_plain(slot((rank + k) % WS, rank) + i, x);
+    for (int u = 0; u < U; ++u) {
+      const int64_t i = i0 + static_cast<int64_t>(u) * blockDim.x;
+      if (i < end) x[u] = ld_plain(src + i);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t i = i0 + static_cast<int64_t>(u) * blockDim.x;
+      if (i < end) {
+#pragma unroll
+        for (int k = 1; k < WS; ++k) st_plain(slot((rank + k) % WS, rank) + i, x[u]);
+      }
+    }
   }
   int peers[WS > 1 ? WS - 1 : 1];
   all_peers<WS>(rank, peers);
@@ -103,15 +125,27 @@ __global__ void __launch_bounds__(kThreads) k_oneshot(const __grid_constant__ AR
   // 2. reduce all WS contributions in rank order
   if (ok) {
     uint4* dst = reinterpret_cast<uint4*>(me.out);
-    for (int64_t i = beg + threadIdx.x; i < end; i += blockDim.x) {
-      uint4 x[WS];
+    for (int64_t i0 = beg + threadIdx.x; i0 < end; i0 += static_cast<int64_t>(blockDim.x) * UR) {
+      uint4 x[UR][WS];
 #pragma unroll
-      for (int q = 0; q < WS; ++q) x[q] = (q == rank) ? ld_plain(src + i) : ld_cg(slot(rank, q) + i);
-      Acc<T> a;
-      acc_set(a, x[0]);
+      for (int u = 0; u < UR; ++u) {
+        const int64_t i = i0 + static_cast<int64_t>(u) * blockDim.x;
+        if (i < end) {
 #pragma unroll
-      for (int q = 1; q < WS; ++q) acc_add(a, x[q]);
-      st_plain(dst + i, acc_pack(a));
+          for (int q = 0; q < WS; ++q) x[u][q] = (q == rank) ? ld_plain(src + i) : ld_cg(slot(rank, q) + i);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < UR; ++u) {
+        const int64_t i = i0 + static_cast<int64_t>(u) * blockDim.x;
+        if (i < end) {
+          Acc<T> a;
+          acc_set(a, x[u][0]);
+#pragma unroll
+          for (int q = 1; q < WS; ++q) acc_add(a, x[u][q]);
+          st_plain(dst + i, acc_pack(a));
+        }
+      }
     }
   }
   end_call(me, epoch);
@@ -119,7 +153,9 @@ __global__ void __launch_bounds__(kThreads) k_oneshot(const __grid_constant__ AR
 
 // --------------------------------------------------------------- twoshot ----
 template <typename T, int WS>
-__global__ void __launch_bounds__(kThreads) k_twoshot(const __grid_constant__ ARParams p) {
+__global__ void __launch_bounds__(kThreads, 1) k_twoshot(const __grid_constant__ ARParams p) {
+  constexpr int UP = Unroll<WS>::kPeer;
+  constexpr int UR = Unroll<WS>::kRed;
   const RankView& me = p.v[blockIdx.y];
   const int rank = me.rank;
   const uint32_t epoch = begin_call(me);
@@ -128,67 +164,105 @@ __global__ void __launch_bounds__(kThreads) k_twoshot(const __grid_constant__ AR
   const int chp = p.chunk_packs;
   const int64_t tile = static_cast<int64_t>(WS) * chp;
   const int64_t stripe = tile * gridDim.x;
-  const int64_t cta_packs = (WS + 1) * (p.L.chunk_max / 16);
+  const int64_t slot_stride = p.L.chunk_max / 16;
+  const int64_t cta_packs = (WS + 1) * slot_stride;
   const uint4* src = reinterpret_cast<const uint4*>(me.in);
   uint4* dst = reinterpret_cast<uint4*>(me.out);
   // CTA c's region in rank r's workspace: [WS rs slots][result]
   auto region = [&](int r) -> uint4* {
     return reinterpret_cast<uint4*>(me.wsp[r] + p.L.twoshot_off) + c * cta_packs;
   };
-  const int64_t slot_stride = p.L.chunk_max / 16;
   int peers[WS - 1];
   all_peers<WS>(rank, peers);
+  const int stride = blockDim.x;
   bool ok = true;
   for (int r = 0; r < p.rounds && ok; ++r) {
     const int64_t tbase = r * stripe + c * tile;
     const uint64_t seq = make_seq(epoch, r + 1);
+    // valid packs of each owner's chunk in this round (the last round is ragged)
+    auto chunk_len = [&](int owner) -> int {
+      const int64_t b = tbase + static_cast<int64_t>(owner) * chp;
+      return static_cast<int>(span_len(chp, p.npacks - b));
+    };
     // 1. reduce-scatter by stores: chunk j -> owner j, slot [rank]
-    for (int i = threadIdx.x; i < chp; i += blockDim.x) {
-      uint4 x[WS - 1];
+    {
+      int len[WS - 1];
 #pragma unroll
-      for (int k = 0; k < WS - 1; ++k) {
-        const int64_t g = tbase + static_cast<int64_t>(peers[k]) * chp + i;
-        if (g < p.npacks) x[k] = ld_plain(src + g);
-      }
+      for (int k = 0; k < WS - 1; ++k) len[k] = chunk_len(peers[k]);
+      for (int i0 = threadIdx.x; i0 < chp; i0 += stride * UP) {
+        uint4 x[UP][WS - 1];
 #pragma unroll
-      for (int k = 0; k < WS - 1; ++k) {
-        const int64_t g = tbase + static_cast<int64_t>(peers[k]) * chp + i;
-        if (g < p.npacks) st_plain(region(peers[k]) + rank * slot_stride + i, x[k]);
+        for (int u = 0; u < UP; ++u) {
+          const int i = i0 + u * stride;
+#pragma unroll
+          for (int k = 0; k < WS - 1; ++k)
+            if (i < len[k]) x[u][k] = ld_plain(src + tbase + static_cast<int64_t>(peers[k]) * chp + i);
+        }
+#pragma unroll
+        for (int u = 0; u < UP; ++u) {
+          const int i = i0 + u * stride;
+#pragma unroll
+          for (int k = 0; k < WS - 1; ++k)
+            if (i < len[k]) st_plain(region(peers[k]) + rank * slot_stride + i, x[u][k]);
+        }
       }
     }
     ok = exchange(me, kFlagRS, c, seq, peers, WS - 1, w, kStageRS);
     if (!ok) break;
     // 2. reduce my chunk; publish it in my result slot and in my output
-    uint4* mine = region(rank);
-    for (int i = threadIdx.x; i < chp; i += blockDim.x) {
-      const int64_t g = tbase + static_cast<int64_t>(rank) * chp + i;
-      if (g < p.npacks) {
-        uint4 x[WS];
+    {
+      uint4* mine = region(rank);
+      const int mlen = chunk_len(rank);
+      const int64_t mbase = tbase + static_cast<int64_t>(rank) * chp;
+      for (int i0 = threadIdx.x; i0 < mlen; i0 += stride * UR) {
+        uint4 x[UR][WS];
 #pragma unroll
-        for (int q = 0; q < WS; ++q) x[q] = (q == rank) ? ld_plain(src + g) : ld_cg(mine + q * slot_stride + i);
-        Acc<T> a;
-        acc_set(a, x[0]);
+        for (int u = 0; u < UR; ++u) {
+          const int i = i0 + u * stride;
+          if (i < mlen) {
 #pragma unroll
-        for (int q = 1; q < WS; ++q) acc_add(a, x[q]);
-        const uint4 y = acc_pack(a);
-        st_plain(mine + WS * slot_stride + i, y);
-        st_plain(dst + g, y);
+            for (int q = 0; q < WS; ++q)
+              x[u][q] = (q == rank) ? ld_plain(src + mbase + i) : ld_cg(mine + q * slot_stride + i);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < UR; ++u) {
+          const int i = i0 + u * stride;
+          if (i < mlen) {
+            Acc<T> a;
+            acc_set(a, x[u][0]);
+#pragma unroll
+            for (int q = 1; q < WS; ++q) acc_add(a, x[u][q]);
+            const uint4 y = acc_pack(a);
+            st_plain(mine + WS * slot_stride + i, y);
+            st_plain(dst + mbase + i, y);
+          }
+        }
       }
     }
     ok = exchange(me, kFlagAG, c, seq, peers, WS - 1, w, kStageAG);
     if (!ok) break;
     // 3. all-gather by loads from every owner's result slot
-    for (int i = threadIdx.x; i < chp; i += blockDim.x) {
-      uint4 x[WS - 1];
+    {
+      int len[WS - 1];
 #pragma unroll
-      for (int k = 0; k < WS - 1; ++k) {
-        const int64_t g = tbase + static_cast<int64_t>(peers[k]) * chp + i;
-        if (g < p.npacks) x[k] = ld_cg(region(peers[k]) + WS * slot_stride + i);
-      }
+      for (int k = 0; k < WS - 1; ++k) len[k] = chunk_len(peers[k]);
+      for (int i0 = threadIdx.x; i0 < chp; i0 += stride * UP) {
+        uint4 x[UP][WS - 1];
 #pragma unroll
-      for (int k = 0; k < WS - 1; ++k) {
-        const int64_t g = tbase + static_cast<int64_t>(peers[k]) * chp + i;
-        if (g < p.npacks) st_plain(dst + g, x[k]);
+        for (int u = 0; u < UP; ++u) {
+          const int i = i0 + u * stride;
+#pragma unroll
+          for (int k = 0; k < WS - 1; ++k)
+            if (i < len[k]) x[u][k] = ld_cg(region(peers[k]) + WS * slot_stride + i);
+        }
+#pragma unroll
+        for (int u = 0; u < UP; ++u) {
+          const int i = i0 + u * stride;
+#pragma unroll
+          for (int k = 0; k < WS - 1; ++k)
+            if (i < len[k]) st_plain(dst + tbase + static_cast<int64_t>(peers[k]) * chp + i, x[u][k]);
+        }
       }
     }
   }
@@ -197,12 +271,13 @@ __global__ void __launch_bounds__(kThreads) k_twoshot(const __grid_constant__ AR
 
 // ------------------------------------------------------------------ hier ----
 // Stage 1: reduce-scatter inside the group (chunk l -> local index l).
-// Stage 2: the owners of chunk l in all groups exchange their partial sums
-//          (double-buffered by the CTA's global round parity) and each adds
-//          them in group order.
+// Stage 2: the owners of chunk l in all groups exchange their partial sums in
+//          fp32 (double-buffered by the CTA's global round parity) and each
+//          adds them in group order, so the result is rounded exactly once.
 // Stage 3: all-gather inside the group by loads.
 template <typename T>
 __global__ void __launch_bounds__(kThreads) k_hier(const __grid_constant__ ARParams p) {
+  constexpr int XW = AccWords<T>::kW;
   const RankView& me = p.v[blockIdx.y];
   const int rank = me.rank;
   const uint32_t epoch = begin_call(me);
@@ -213,15 +288,16 @@ __global__ void __launch_bounds__(kThreads) k_hier(const __grid_constant__ ARPar
   const int chp = p.chunk_packs;
   const int64_t tile = static_cast<int64_t>(G) * chp;
   const int64_t stripe = tile * gridDim.x;
-  const int64_t slot_stride = p.L.chunk_max / 16;
-  const int64_t cta_packs = (G + 2 * NG + 1) * slot_stride;
+  const int64_t slot_stride = p.L.hier_chunk / 16;
+  // per CTA: [G rs slots][2 parities x NG groups x 2 widths of fp32 partials][result]
+  const int64_t cta_packs = (G + 4 * NG + 1) * slot_stride;
+  const int64_t res_off = (G + 4 * NG) * slot_stride;
   const uint4* src = reinterpret_cast<const uint4*>(me.in);
   uint4* dst = reinterpret_cast<uint4*>(me.out);
   auto region = [&](int r) -> uint4* {
     return reinterpret_cast<uint4*>(me.wsp[r] + p.L.hier_off) + c * cta_packs;
   };
-  // slots: [0,G) rs by source local index, [G, G+2NG) x by parity*NG + source
-  // group, [G+2NG] result.
+  auto xslot = [&](int par, int h) -> int64_t { return (G + 2 * (par * NG + h)) * slot_stride; };
   int gpeers[kMaxRanks], xpeers[kMaxRanks];
   int ng = 0, nx = 0;
   for (int m = 0; m < G; ++m)
@@ -233,8 +309,7 @@ __global__ void __launch_bounds__(kThreads) k_hier(const __grid_constant__ ARPar
   __syncthreads();
   const uint32_t base_rounds = s_base;
   bool ok = true;
-  int r = 0;
-  for (; r < p.rounds && ok; ++r) {
+  for (int r = 0; r < p.rounds && ok; ++r) {
     const int64_t tbase = r * stripe + c * tile;
     const uint64_t seq = make_seq(epoch, r + 1);
     const int par = (base_rounds + r) & 1;
@@ -248,7 +323,7 @@ __global__ void __launch_bounds__(kThreads) k_hier(const __grid_constant__ ARPar
     }
     ok = exchange(me, kFlagHierRS, c, seq, gpeers, ng, w, kStageRS);
     if (!ok) break;
-    // 2a. group partial of chunk l -> my own x slot and the same-slice owners
+    // 2a. fp32 group partial of chunk l -> my own slot and the same-slice owners
     uint4* mine = region(rank);
     for (int i = threadIdx.x; i < chp; i += blockDim.x) {
       const int64_t gi = tbase + static_cast<int64_t>(l) * chp + i;
@@ -258,26 +333,22 @@ __global__ void __launch_bounds__(kThreads) k_hier(const __grid_constant__ ARPar
           const uint4 x = (m == l) ? ld_plain(src + gi) : ld_cg(mine + m * slot_stride + i);
           if (m == 0) acc_set(a, x); else acc_add(a, x);
         }
-        const uint4 part = acc_pack(a);
-        const int64_t xs = (G + par * NG + g) * slot_stride + i;
-        st_plain(mine + xs, part);
+        const int64_t xs = xslot(par, g) + static_cast<int64_t>(i) * XW;
+        acc_store_f32(mine + xs, a);
         for (int h = 0; h < NG; ++h)
-          if (h != g) st_plain(region(p.member[h][l]) + xs, part);
+          if (h != g) acc_store_f32(region(p.member[h][l]) + xs, a);
       }
     }
     ok = exchange(me, kFlagHierX, c, seq, xpeers, nx, w, kStageHierX);
     if (!ok) break;
-    // 2b. sum the group partials in group order -> result slot and output
+    // 2b. add the group partials in group order, round once -> result slot and output
     for (int i = threadIdx.x; i < chp; i += blockDim.x) {
       const int64_t gi = tbase + static_cast<int64_t>(l) * chp + i;
       if (gi < p.npacks) {
         Acc<T> a;
-        for (int h = 0; h < NG; ++h) {
-          const uint4 x = ld_cg(mine + (G + par * NG + h) * slot_stride + i);
-          if (h == 0) acc_set(a, x); else acc_add(a, x);
-        }
+        for (int h = 0; h < NG; ++h) acc_accum_f32(a, mine + xslot(par, h) + static_cast<int64_t>(i) * XW, h == 0);
         const uint4 y = acc_pack(a);
-        st_plain(mine + (G + 2 * NG) * slot_stride + i, y);
+        st_plain(mine + res_off + i, y);
         st_plain(dst + gi, y);
       }
     }
@@ -288,8 +359,7 @@ __global__ void __launch_bounds__(kThreads) k_hier(const __grid_constant__ ARPar
       for (int m = 0; m < G; ++m) {
         if (m == l) continue;
         const int64_t gi = tbase + static_cast<int64_t>(m) * chp + i;
-        if (gi < p.npacks)
-          st_plain(dst + gi, ld_cg(region(p.member[g][m]) + (G + 2 * NG) * slot_stride + i));
+        if (gi < p.npacks) st_plain(dst + gi, ld_cg(region(p.member[g][m]) + res_off + i));
       }
     }
   }
@@ -333,7 +403,8 @@ __global__ void __launch_bounds__(kThreads) k_oneshot_pull(const __grid_constant
 
 // ---------------------------------------------------------- NVLS oneshot ----
 template <typename T, int WS>
-__global__ void __launch_bounds__(kThreads) k_nvls_oneshot(const __grid_constant__ ARParams p) {
+__global__ void __launch_bounds__(kThreads, 2) k_nvls_oneshot(const __grid_constant__ ARParams p) {
+  constexpr int U = 4;
   const RankView& me = p.v[blockIdx.y];
   const uint32_t epoch = begin_call(me);
   const WaitCtx w = make_wait(p, me, epoch);
@@ -349,25 +420,46 @@ __global__ void __launch_bounds__(kThreads) k_nvls_oneshot(const __grid_constant
   const uint4* mc = reinterpret_cast<const uint4*>(me.mc + off);
   NvlsPad* upad = reinterpret_cast<NvlsPad*>(me.uc);
   NvlsPad* mpad = reinterpret_cast<NvlsPad*>(me.mc);
-  for (int64_t i = beg + threadIdx.x; i < end; i += blockDim.x) st_plain(uc + i, ld_plain(src + i));
+  const int64_t stride = blockDim.x;
+  for (int64_t i0 = beg + threadIdx.x; i0 < end; i0 += stride * U) {
+    uint4 x[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (i0 + u * stride < end) x[u] = ld_plain(src + i0 + u * stride);
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (i0 + u * stride < end) st_plain(uc + i0 + u * stride, x[u]);
+  }
+  fence_proxy_alias();  // unicast stores before the multicast arrival
   __syncthreads();
   __shared__ int s_ok;
   if (threadIdx.x == 0) {
     const uint32_t calls = upad->rounds[b][1] + 1u;
-    mm_red_add_release(&mpad->cnt[b][0][0], 1u);
-    s_ok = wait_geq_u32(&upad->cnt[b][0][0], calls * WS, w, kStageNvls1);
+    mm_red_add_release(&mpad->cnt[b][2][0], 1u);
+    s_ok = wait_geq_u32(&upad->cnt[b][2][0], calls * WS, w, kStageNvls1);
     upad->rounds[b][1] = calls;
   }
   __syncthreads();
+  fence_proxy_alias();  // unicast acquire before multicast loads
   if (s_ok) {
-    for (int64_t i = beg + threadIdx.x; i < end; i += blockDim.x) st_plain(dst + i, mm_ld_reduce<T>(mc + i));
+    for (int64_t i0 = beg + threadIdx.x; i0 < end; i0 += stride * U) {
+      uint4 y[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (i0 + u * stride < end) y[u] = mm_ld_reduce<T>(mc + i0 + u * stride);
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (i0 + u * stride < end) st_plain(dst + i0 + u * stride, y[u]);
+    }
   }
   end_call(me, epoch);
 }
 
 // ---------------------------------------------------------- NVLS twoshot ----
 template <typename T, int WS>
-__global__ void __launch_bounds__(kThreads) k_nvls_twoshot(const __grid_constant__ ARParams p) {
+__global__ void __launch_bounds__(kThreads, 1) k_nvls_twoshot(const __grid_constant__ ARParams p) {
+  constexpr int U = 8;
+  constexpr int UL = 4;
   const RankView& me = p.v[blockIdx.y];
   const int rank = me.rank;
   const uint32_t epoch = begin_call(me);
@@ -384,6 +476,7 @@ __global__ void __launch_bounds__(kThreads) k_nvls_twoshot(const __grid_constant
   NvlsPad* mpad = reinterpret_cast<NvlsPad*>(me.mc);
   const uint4* src = reinterpret_cast<const uint4*>(me.in);
   uint4* dst = reinterpret_cast<uint4*>(me.out);
+  const int stride = blockDim.x;
   __shared__ uint32_t s_base;
   __shared__ int s_ok;
   if (threadIdx.x == 0) s_base = upad->rounds[c][0];
@@ -393,44 +486,71 @@ __global__ void __launch_bounds__(kThreads) k_nvls_twoshot(const __grid_constant
   for (int r = 0; r < p.rounds && ok; ++r) {
     const int64_t tbase = r * stripe + c * tile;
     const uint32_t target = (base + r + 1u) * WS;
-    // 1. copy the whole tile in (every chunk)
-    for (int j = 0; j < WS; ++j) {
-      for (int i = threadIdx.x; i < chp; i += blockDim.x) {
-        const int64_t g = tbase + static_cast<int64_t>(j) * chp + i;
-        if (g < p.npacks) st_plain(uc + j * slot_stride + i, ld_plain(src + g));
+    const int tlen = static_cast<int>(span_len(tile, p.npacks - tbase));
+    // 1. copy the whole tile in; chunk j lives at uc + j * slot_stride
+    for (int i0 = threadIdx.x; i0 < tlen; i0 += stride * U) {
+      uint4 x[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (i0 + u * stride < tlen) x[u] = ld_plain(src + tbase + i0 + u * stride);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = i0 + u * stride;
+        if (i < tlen) st_plain(uc + (i / chp) * slot_stride + (i % chp), x[u]);
       }
     }
+    fence_proxy_alias();  // unicast stores before the multicast arrival
     __syncthreads();
     if (threadIdx.x == 0) {
       mm_red_add_release(&mpad->cnt[c][0][0], 1u);
       s_ok = wait_geq_u32(&upad->cnt[c][0][0], target, w, kStageNvls1);
     }
     __syncthreads();
+    fence_proxy_alias();  // unicast acquire before multicast loads
     ok = s_ok;
     if (!ok) break;
     // 2. reduce my chunk in the switch and broadcast the result
-    for (int i = threadIdx.x; i < chp; i += blockDim.x) {
-      const int64_t g = tbase + static_cast<int64_t>(rank) * chp + i;
-      if (g < p.npacks) {
-        const uint4 y = mm_ld_reduce<T>(mc + rank * slot_stride + i);
-        mm_st<T>(mc + rank * slot_stride + i, y);
-        st_plain(dst + g, y);
+    {
+      const int64_t mbase = tbase + static_cast<int64_t>(rank) * chp;
+      const int mlen = static_cast<int>(span_len(chp, p.npacks - mbase));
+      uint4* mchunk = mc + rank * slot_stride;
+      for (int i0 = threadIdx.x; i0 < mlen; i0 += stride * UL) {
+        uint4 y[UL];
+#pragma unroll
+        for (int u = 0; u < UL; ++u)
+          if (i0 + u * stride < mlen) y[u] = mm_ld_reduce<T>(mchunk + i0 + u * stride);
+#pragma unroll
+        for (int u = 0; u < UL; ++u) {
+          const int i = i0 + u * stride;
+          if (i < mlen) {
+            mm_st<T>(mchunk + i, y[u]);
+            st_plain(dst + mbase + i, y[u]);
+          }
+        }
       }
     }
+    fence_proxy_alias();
     __syncthreads();
     if (threadIdx.x == 0) {
       mm_red_add_release(&mpad->cnt[c][1][0], 1u);
       s_ok = wait_geq_u32(&upad->cnt[c][1][0], target, w, kStageNvls2);
     }
     __syncthreads();
+    fence_proxy_alias();  // multicast stores of the peers before unicast loads
     ok = s_ok;
     if (!ok) break;
     // 3. copy the other owners' results out of my local copy
-    for (int j = 0; j < WS; ++j) {
-      if (j == rank) continue;
-      for (int i = threadIdx.x; i < chp; i += blockDim.x) {
-        const int64_t g = tbase + static_cast<int64_t>(j) * chp + i;
-        if (g < p.npacks) st_plain(dst + g, ld_cg(uc + j * slot_stride + i));
+    for (int i0 = threadIdx.x; i0 < tlen; i0 += stride * U) {
+      uint4 x[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = i0 + u * stride;
+        if (i < tlen && i / chp != rank) x[u] = ld_cg(uc + (i / chp) * slot_stride + (i % chp));
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = i0 + u * stride;
+        if (i < tlen && i / chp != rank) st_plain(dst + tbase + i, x[u]);
       }
     }
   }

@@ -28,10 +28,12 @@ T clampv(T v, T lo, T hi) {
 
 std::string cuda_error_string(cudaError_t e) { return cudaGetErrorString(e); }
 
+// Entry points are requested as of CUDA 12.5: the multicast (NVLS) calls
+// appeared in 12.1, so an older version would report them as missing.
 void* driver_entry(const char* name) {
   void* fn = nullptr;
   cudaDriverEntryPointQueryResult q;
-  cudaError_t e = cudaGetDriverEntryPointByVersion(name, &fn, 12000, cudaEnableDefault, &q);
+  cudaError_t e = cudaGetDriverEntryPointByVersion(name, &fn, 12050, cudaEnableDefault, &q);
   if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr)
     throw std::runtime_error(std::string("CUDA driver entry point unavailable: ") + name);
   return fn;
@@ -52,20 +54,29 @@ Layout make_layout(int ws, const CommConfig& cfg) {
   if (cfg.max_ctas < 1 || cfg.max_ctas > kMaxBlocks || cfg.oneshot_ctas < 1 ||
       cfg.oneshot_ctas > kMaxBlocks)
     throw std::invalid_argument("CTA counts must be in [1, 160]");
-  if (cfg.chunk_max < 16 * 512 || cfg.chunk_max % 16 != 0)
-    throw std::invalid_argument("chunk_max must be a multiple of 16 and >= 8 KiB");
+  if (cfg.chunk_max != 0 && (cfg.chunk_max < 16 * 512 || cfg.chunk_max % 16 != 0))
+    throw std::invalid_argument("chunk_max must be 0 (auto) or a multiple of 16 and >= 8 KiB");
   if (cfg.oneshot_max % 16 != 0) throw std::invalid_argument("oneshot_max must be a multiple of 16");
   Layout L{};
   int64_t off = round_up(static_cast<int64_t>(sizeof(SignalPad)), kAlign);
   L.oneshot_off = off;
   L.oneshot_max = cfg.oneshot_max;
   off += round_up(2 * ws * cfg.oneshot_max, kAlign);
-  L.chunk_max = cfg.chunk_max;
+  const int64_t chunk = cfg.chunk_max != 0
+                            ? cfg.chunk_max
+                            : std::max<int64_t>(32 << 10, std::min<int64_t>(256 << 10, (512 << 10) / ws / 4096 * 4096));
+  L.chunk_max = chunk;
   L.max_ctas = cfg.max_ctas;
   L.twoshot_off = off;
-  off += round_up(static_cast<int64_t>(cfg.max_ctas) * (ws + 1) * cfg.chunk_max, kAlign);
+  off += round_up(static_cast<int64_t>(cfg.max_ctas) * (ws + 1) * chunk, kAlign);
+  // The hierarchical protocol exists to cut cross-group traffic, not for peak
+  // bandwidth on NVSwitch, so it gets a smaller region: at most 64 CTAs and
+  // 32 KiB chunks. Per CTA: gsize rs slots + 2 parities x ngroups fp32 partial
+  // slots (two chunk widths each) + 1 result; gsize + 4 * ngroups + 1 <= 4 * ws + 2.
+  L.hier_ctas = std::min(cfg.max_ctas, 64);
+  L.hier_chunk = std::min<int64_t>(chunk, 32 << 10);
   L.hier_off = off;
-  off += round_up(static_cast<int64_t>(cfg.max_ctas) * (2 * ws + 2) * cfg.chunk_max, kAlign);
+  off += round_up(static_cast<int64_t>(L.hier_ctas) * (4 * ws + 2) * L.hier_chunk, kAlign);
   L.fused_off = off;
   L.fused_bytes = round_up(cfg.fused_bytes, kAlign);
   off += 2 * ws * L.fused_bytes;
@@ -76,7 +87,7 @@ Layout make_layout(int ws, const CommConfig& cfg) {
   L.mc_oneshot_off = moff;
   moff += round_up(2 * cfg.oneshot_max, kAlign);
   L.mc_twoshot_off = moff;
-  moff += round_up(static_cast<int64_t>(cfg.max_ctas) * ws * cfg.chunk_max, kAlign);
+  moff += round_up(static_cast<int64_t>(cfg.max_ctas) * ws * chunk, kAlign);
   L.mc_bytes = moff;
   return L;
 }
@@ -217,6 +228,10 @@ LaunchPlan Communicator::plan(int64_t nbytes, int algo, bool registered) const {
     else
       algo = kAlgoTwoshot;
   }
+  if ((algo == kAlgoNvlsOneshot || algo == kAlgoNvlsTwoshot) && mc_ == nullptr)
+    throw std::invalid_argument("NVLS protocol requested but no multicast workspace attached");
+  if (algo == kAlgoHier && ngroups_ == 0)
+    throw std::invalid_argument("hierarchical protocol requested but no groups set");
   pl.algo = algo;
   switch (algo) {
     case kAlgoOneshot:
@@ -231,10 +246,11 @@ LaunchPlan Communicator::plan(int64_t nbytes, int algo, bool registered) const {
     case kAlgoTwoshot:
     case kAlgoNvlsTwoshot:
     case kAlgoHier: {
-      const int parts = (algo == kAlgoHier) ? gsize_ : ws_;
-      const int64_t chunk_cap = L_.chunk_max / 16;
+      const bool hier = algo == kAlgoHier;
+      const int parts = hier ? gsize_ : ws_;
+      const int64_t chunk_cap = (hier ? L_.hier_chunk : L_.chunk_max) / 16;
       const int64_t C = clampv<int64_t>(ceil_div_host(npacks, static_cast<int64_t>(parts) * 512), 1,
-                                        cfg_.max_ctas);
+                                        hier ? L_.hier_ctas : cfg_.max_ctas);
       const int64_t chp = std::min(chunk_cap, std::max<int64_t>(1, ceil_div_host(npacks, C * parts)));
       const int64_t rounds = ceil_div_host(npacks, C * parts * chp);
       if (rounds >= (int64_t(1) << kSeqShift)) throw std::invalid_argument("message too large");
@@ -246,10 +262,6 @@ LaunchPlan Communicator::plan(int64_t nbytes, int algo, bool registered) const {
     default:
       throw std::invalid_argument("unknown allreduce algorithm " + std::to_string(algo));
   }
-  if ((algo == kAlgoNvlsOneshot || algo == kAlgoNvlsTwoshot) && mc_ == nullptr)
-    throw std::invalid_argument("NVLS protocol requested but no multicast workspace attached");
-  if (algo == kAlgoHier && ngroups_ == 0)
-    throw std::invalid_argument("hierarchical protocol requested but no groups set");
   return pl;
 }
 
@@ -364,7 +376,8 @@ int emulate_allreduce(const std::vector<Communicator*>& comms, cudaStream_t s,
       ARParams tmp{};
       c0->fill_params(tmp, pl, nbytes);
       const int parts = (pl.algo == kAlgoHier) ? tmp.gsize : ws;
-      const int64_t chunk_cap = c0->layout().chunk_max / 16;
+      const int64_t chunk_cap =
+          (pl.algo == kAlgoHier ? c0->layout().hier_chunk : c0->layout().chunk_max) / 16;
       const int64_t chp = std::min(chunk_cap, std::max<int64_t>(1, ceil_div_host(npacks, cap * parts)));
       pl.chunk_packs = static_cast<int>(chp);
       pl.rounds = static_cast<int>(ceil_div_host(npacks, cap * parts * chp));

@@ -26,8 +26,10 @@ namespace nab {
 
 struct CommConfig {
   int64_t oneshot_max = 1 << 20;  // largest message of the one-shot protocols
-  int64_t chunk_max = 64 << 10;   // bytes per owner chunk per round
-  int max_ctas = 64;              // CTAs of the tiled protocols
+  // Bytes per owner chunk per round of the two-shot protocols; 0 picks
+  // 512 KiB / world size (a CTA moves ~512 KiB per round at any world size).
+  int64_t chunk_max = 0;
+  int max_ctas = 128;             // CTAs of the tiled protocols
   int oneshot_ctas = 32;          // CTAs of the one-shot protocols
   int64_t fused_bytes = 512 << 10;  // fused one-shot slot (allreduce + norm)
   uint64_t timeout_ns = 5000000000ull;

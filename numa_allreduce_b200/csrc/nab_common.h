@@ -111,7 +111,10 @@ struct alignas(128) SignalPad {
 // every GPU at once with multimem.red; `rounds` is local bookkeeping: how many
 // rounds each CTA index has completed, identical on every rank.
 struct alignas(128) NvlsPad {
-  uint32_t cnt[kMaxBlocks][2][8];  // [cta][phase], 32 B apart
+  // [cta][counter], 32 B apart: 0 and 1 are the two arrival phases of the
+  // two-shot protocol, 2 the one-shot arrival. Each protocol owns its
+  // counters because each tracks its own expected count in `rounds`.
+  uint32_t cnt[kMaxBlocks][3][8];
   uint32_t rounds[kMaxBlocks][2];  // [cta][0]=twoshot rounds, [cta][1]=oneshot calls
 };
 

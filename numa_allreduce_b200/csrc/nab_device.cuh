@@ -113,6 +113,32 @@ NAB_DINLINE uint4 acc_pack(const Acc<__half>& a) {
                     pack_f16x2(a.v[4], a.v[5]), pack_f16x2(a.v[6], a.v[7]));
 }
 
+// fp32 image of an accumulator, as kN / 4 packs (1 for fp32, 2 for 16-bit types).
+template <typename T>
+struct AccWords {
+  static constexpr int kW = VecT<T>::kN / 4;
+};
+
+template <typename T>
+NAB_DINLINE void acc_store_f32(uint4* p, const Acc<T>& a) {
+#pragma unroll
+  for (int w = 0; w < AccWords<T>::kW; ++w)
+    p[w] = make_uint4(__float_as_uint(a.v[4 * w]), __float_as_uint(a.v[4 * w + 1]),
+                      __float_as_uint(a.v[4 * w + 2]), __float_as_uint(a.v[4 * w + 3]));
+}
+
+// a = (first ? 0 : a) + the fp32 image at p, read through L2 only.
+template <typename T>
+NAB_DINLINE void acc_accum_f32(Acc<T>& a, const uint4* p, bool first) {
+#pragma unroll
+  for (int w = 0; w < AccWords<T>::kW; ++w) {
+    const uint4 x = __ldcg(p + w);
+    const float f[4] = {__uint_as_float(x.x), __uint_as_float(x.y), __uint_as_float(x.z), __uint_as_float(x.w)};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) a.v[4 * w + e] = first ? f[e] : a.v[4 * w + e] + f[e];
+  }
+}
+
 // --------------------------------------------------------- memory access ----
 // Data loads of buffers that another GPU wrote during this kernel go through
 // L2 only (.cg) so a line cached in L1 by an earlier round is never reused.
@@ -201,6 +227,11 @@ NAB_DINLINE void mm_st<float>(void* mc, uint4 v) {
                "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                : "memory");
 }
+// Orders this thread's accesses made through one virtual alias of a physical
+// location (e.g. the unicast address of the NVLS workspace) with its accesses
+// through another alias of it (the multicast address).
+NAB_DINLINE void fence_proxy_alias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
+
 // Increments the counter at the same offset on every GPU of the multicast
 // object. Release: the CTA's earlier writes (ordered by bar.sync) are visible
 // to any GPU that acquires the incremented value.
@@ -273,6 +304,12 @@ NAB_DINLINE bool wait_geq_u32(const uint32_t* addr, uint32_t target, const WaitC
       }
     }
   }
+}
+
+// min(cap, avail) clamped at 0: the valid length of a ragged last piece.
+NAB_DINLINE int64_t span_len(int64_t cap, int64_t avail) {
+  const int64_t v = cap < avail ? cap : avail;
+  return v > 0 ? v : 0;
 }
 
 template <typename T>

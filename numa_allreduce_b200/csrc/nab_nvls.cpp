@@ -38,7 +38,6 @@ using PFN_Free = CUresult (*)(CUdeviceptr, size_t);
 using PFN_Map = CUresult (*)(CUdeviceptr, size_t, size_t, CUmemGenericAllocationHandle, unsigned long long);
 using PFN_Unmap = CUresult (*)(CUdeviceptr, size_t);
 using PFN_SetAccess = CUresult (*)(CUdeviceptr, size_t, const CUmemAccessDesc*, size_t);
-using PFN_Memset = CUresult (*)(CUdeviceptr, unsigned char, size_t);
 
 CUdevice cu_device(int ordinal) {
   CUdevice d;
@@ -72,24 +71,35 @@ bool nvls_supported(int device) {
   }
 }
 
+static CUmemAllocationProp phys_prop(int device) {
+  CUmemAllocationProp ap{};
+  ap.type = CU_MEM_ALLOCATION_TYPE_PINNED;
+  ap.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+  ap.location.id = device;
+  // same shareable handle type as the multicast object
+  ap.requestedHandleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;
+  return ap;
+}
+
 NvlsBuffer::NvlsBuffer(int device, int world_size, size_t min_bytes)
     : device_(device), ws_(world_size) {
   CUmulticastObjectProp mp{};
   mp.numDevices = static_cast<unsigned>(world_size);
   mp.size = min_bytes;
   mp.handleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;
-  size_t mgran = 0;
-  NAB_CU_CHECK(driver_fn<PFN_McGran>("cuMulticastGetGranularity")(&mgran, &mp,
-                                                                   CU_MULTICAST_GRANULARITY_MINIMUM));
-  CUmemAllocationProp ap{};
-  ap.type = CU_MEM_ALLOCATION_TYPE_PINNED;
-  ap.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
-  ap.location.id = device;
-  size_t agran = 0;
+  NAB_CU_CHECK(driver_fn<PFN_McGran>("cuMulticastGetGranularity")(&mc_gran_, &mp,
+                                                                   CU_MULTICAST_GRANULARITY_RECOMMENDED));
+  const CUmemAllocationProp ap = phys_prop(device);
   NAB_CU_CHECK(driver_fn<PFN_MemGran>("cuMemGetAllocationGranularity")(
-      &agran, &ap, CU_MEM_ALLOC_GRANULARITY_MINIMUM));
-  const size_t gran = std::max(mgran, agran);
+      &alloc_gran_, &ap, CU_MEM_ALLOC_GRANULARITY_RECOMMENDED));
+  const size_t gran = std::max(mc_gran_, alloc_gran_);
   bytes_ = round_up(min_bytes, gran);
+}
+
+std::string NvlsBuffer::describe() const {
+  return "bytes=" + std::to_string(bytes_) + " multicast_granularity=" + std::to_string(mc_gran_) +
+         " allocation_granularity=" + std::to_string(alloc_gran_) + " device=" + std::to_string(device_) +
+         " world=" + std::to_string(ws_);
 }
 
 NvlsBuffer::~NvlsBuffer() {
@@ -129,13 +139,12 @@ void NvlsBuffer::add_device() {
 
 void NvlsBuffer::bind_and_map() {
   if (!added_) throw std::runtime_error("add_device must precede bind_and_map");
-  CUmemAllocationProp ap{};
-  ap.type = CU_MEM_ALLOCATION_TYPE_PINNED;
-  ap.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
-  ap.location.id = device_;
+  const CUmemAllocationProp ap = phys_prop(device_);
   NAB_CU_CHECK(driver_fn<PFN_MemCreate>("cuMemCreate")(&phys_, bytes_, &ap, 0));
   have_phys_ = true;
-  NAB_CU_CHECK(driver_fn<PFN_McBind>("cuMulticastBindMem")(mc_, 0, phys_, 0, bytes_, 0));
+  const CUresult r = driver_fn<PFN_McBind>("cuMulticastBindMem")(mc_, 0, phys_, 0, bytes_, 0);
+  if (r != CUDA_SUCCESS)
+    throw std::runtime_error("cuMulticastBindMem failed: " + cu_error_string(r) + " (" + describe() + ")");
   bound_ = true;
   CUmemAccessDesc ad{};
   ad.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
@@ -153,7 +162,7 @@ void NvlsBuffer::bind_and_map() {
   NAB_CU_CHECK(map(mc, bytes_, 0, mc_, 0));
   NAB_CU_CHECK(access(mc, bytes_, &ad, 1));
   mc_va_ = reinterpret_cast<void*>(mc);
-  NAB_CU_CHECK(driver_fn<PFN_Memset>("cuMemsetD8_v2")(uc, 0, bytes_));
+  NAB_CUDA_CHECK(cudaMemset(uc_va_, 0, bytes_));
   NAB_CUDA_CHECK(cudaDeviceSynchronize());
 }
 

@@ -29,6 +29,7 @@ class NvlsBuffer {
   NvlsBuffer& operator=(const NvlsBuffer&) = delete;
 
   size_t bytes() const { return bytes_; }
+  std::string describe() const;
   // Root only: creates the multicast object and returns a FD that refers to
   // it (owned by this object; the caller sends it to the other ranks).
   int create();
@@ -48,6 +49,7 @@ class NvlsBuffer {
   int device_;
   int ws_;
   size_t bytes_;
+  size_t mc_gran_ = 0, alloc_gran_ = 0;
   CUmemGenericAllocationHandle mc_ = 0;
   CUmemGenericAllocationHandle phys_ = 0;
   bool have_mc_ = false, have_phys_ = false, bound_ = false, added_ = false;

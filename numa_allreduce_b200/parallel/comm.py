@@ -80,7 +80,7 @@ class NumaAwareAllReduce:
     RANK_DATA_BYTES = 8 * 1024 * 1024
 
     def __init__(self, group, device, max_size: int | None = None, enable_optimization: bool = True, *,
-                 oneshot_max: int = 1 << 20, chunk_max: int = 64 << 10, max_ctas: int = 64,
+                 oneshot_max: int = 1 << 20, chunk_max: int = 0, max_ctas: int = 128,
                  oneshot_ctas: int = 32, fused_bytes: int = 512 << 10,
                  hier_groups: list[list[int]] | None = None, topology: NumaTopology | None = None,
                  use_nvls: bool | None = None, timeout_ns: int | None = None,

@@ -60,17 +60,17 @@ def emulate_allreduce(tensor: torch.Tensor, schedule: HierSchedule, group=None) 
     for m, member in enumerate(schedule.groups[g]):
         part = x[a:b] if member == rank else recv1[member]
         acc = part.float().clone() if acc is None else acc + part.float()
-    partial = acc.to(dtype)
+    partial = acc  # fp32: the only rounding happens after stage 2
 
-    # stage 2: same-slice owners of the other groups exchange partial sums
+    # stage 2: same-slice owners of the other groups exchange fp32 partial sums
     peers2 = schedule.stage2_peers(rank)
-    recv2 = _exchange({p: partial for p in peers2}, {p: (b - a, dtype) for p in peers2}, group)
+    recv2 = _exchange({p: partial for p in peers2}, {p: (b - a, torch.float32) for p in peers2}, group)
     acc = None
     for h in range(schedule.ngroups):
         owner = schedule.member(h, l)
         part = partial if owner == rank else recv2[owner]
-        acc = part.float().clone() if acc is None else acc + part.float()
-    final = acc.to(dtype) if schedule.ngroups > 1 else partial
+        acc = part.clone() if acc is None else acc + part
+    final = acc.to(dtype)
 
     # stage 3: intra-group all-gather
     out = torch.empty_like(x)

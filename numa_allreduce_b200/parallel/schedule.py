@@ -19,8 +19,9 @@ stage 3 really gathers from peers.
 
 The CPU emulator (:mod:`.emulate`) executes these objects over a gloo group,
 the CUDA kernels implement the same arithmetic (fp32 accumulation in local
-order, partial sums rounded to the input dtype, then summed in group order),
-and :func:`reference_allreduce` computes the exact result both must give.
+order, group partial sums kept in fp32 and added in group order, one
+rounding to the input dtype at the end), and :func:`reference_allreduce`
+computes the exact result both must give.
 """
 
 from __future__ import annotations
@@ -123,14 +124,10 @@ class HierSchedule:
         return (self.ngroups - 1) * -(-nbytes // self.gsize)
 
 
-def _round(x32: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
-    return x32.to(dtype)
-
-
 def reference_allreduce(inputs: list[torch.Tensor], schedule: HierSchedule) -> torch.Tensor:
     """Exact result of the schedule's arithmetic: per group, fp32 sum in local
-    order rounded to the input dtype; then fp32 sum of the group partials in
-    group order, rounded once more."""
+    order; then fp32 sum of the group partials in group order; one rounding
+    to the input dtype."""
     if len(inputs) != schedule.world_size:
         raise ValueError("one input per rank")
     dtype = inputs[0].dtype
@@ -139,10 +136,8 @@ def reference_allreduce(inputs: list[torch.Tensor], schedule: HierSchedule) -> t
         acc = inputs[g[0]].float().clone()
         for r in g[1:]:
             acc += inputs[r].float()
-        partials.append(_round(acc, dtype))
-    if len(partials) == 1:
-        return partials[0]
-    acc = partials[0].float().clone()
+        partials.append(acc)
+    acc = partials[0]
     for p in partials[1:]:
-        acc += p.float()
-    return _round(acc, dtype)
+        acc = acc + p
+    return acc.to(dtype)

@@ -53,73 +53,132 @@ def pci_bus_id(device: int) -> str:
     return f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0".upper()
 
 
-class ClockSampler:
-    """Samples nvidia-smi clocks and throttle reasons every 200 ms while active.
+# NVML clock-event reason bits (nvmlClocksEventReason*), public NVML API values.
+_NVML_REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+                 "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80}
 
-    ``stop()`` returns ``{"sm_mhz": median, "sm_max_mhz": ..., "power_w_max":
-    ..., "reasons": [...], "samples": n}`` for the GPUs whose PCI bus ids were
-    given (all GPUs if none). Nothing is changed on the GPU: it only reads.
+
+def _summarise(rows: list[tuple[float, float, float, set]]) -> dict:
+    if not rows:
+        return {"available": False}
+    reasons = set()
+    for r in rows:
+        reasons |= r[3]
+    return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+            "power_w_max": round(max(r[2] for r in rows), 1), "reasons": sorted(reasons), "samples": len(rows)}
+
+
+class ClockSampler:
+    """Samples SM clocks, power and throttle reasons while active.
+
+    Polls NVML from a background thread every ``interval_ms`` (a few ms, so a
+    short timed region still gets samples); without NVML it runs
+    ``nvidia-smi --loop-ms``. ``stop()`` returns ``{"sm_mhz": median,
+    "sm_max_mhz", "power_w_max", "reasons": [...], "samples"}`` over the GPUs
+    whose PCI bus ids were given. It only reads; nothing on the GPU changes.
     """
 
-    def __init__(self, bus_ids: list[str] | None = None, interval_ms: int = 200):
-        self.bus_ids = {b.upper().lstrip("0") for b in bus_ids} if bus_ids else None
+    def __init__(self, bus_ids: list[str] | None = None, interval_ms: int = 5):
+        self.bus_ids = list(bus_ids) if bus_ids else []
         self.interval_ms = interval_ms
-        self.proc = None
-        self.path = None
+        self._thread = None
+        self._stop = None
+        self._rows: list = []
+        self._smi = None
+        self._path = None
 
     def start(self) -> "ClockSampler":
-        fd, self.path = tempfile.mkstemp(prefix="nab_clocks_", suffix=".csv")
+        try:
+            import threading
+
+            import pynvml
+
+            pynvml.nvmlInit()
+            if self.bus_ids:
+                handles = [pynvml.nvmlDeviceGetHandleByPciBusId(b) for b in self.bus_ids]
+            else:
+                handles = [pynvml.nvmlDeviceGetHandleByIndex(i) for i in range(pynvml.nvmlDeviceGetCount())]
+            get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+            self._stop = threading.Event()
+
+            def sample():
+                for h in handles:
+                    sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                    mx = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+                    pw = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+                    bits = int(get_reasons(h))
+                    self._rows.append((sm, mx, pw, {k for k, b in _NVML_REASONS.items() if bits & b}))
+
+            def loop():
+                while not self._stop.is_set():
+                    try:
+                        sample()
+                    except Exception:
+                        return
+                    self._stop.wait(self.interval_ms / 1000.0)
+                try:
+                    sample()
+                except Exception:
+                    pass
+
+            sample()
+            self._thread = threading.Thread(target=loop, daemon=True)
+            self._thread.start()
+            return self
+        except Exception:
+            self._thread = None
+        fd, self._path = tempfile.mkstemp(prefix="nab_clocks_", suffix=".csv")
         os.close(fd)
         try:
-            self.proc = subprocess.Popen(
+            self._smi = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={CLOCK_FIELDS}", "--format=csv,noheader,nounits",
-                 f"--loop-ms={self.interval_ms}", f"--filename={self.path}"],
+                 f"--loop-ms={max(100, self.interval_ms)}", f"--filename={self._path}"],
                 stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
         except (OSError, ValueError):
-            self.proc = None
+            self._smi = None
         return self
 
     def stop(self) -> dict:
-        if self.proc is None:
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
+            try:
+                import pynvml
+
+                pynvml.nvmlShutdown()
+            except Exception:
+                pass
+            out = _summarise(self._rows)
+            out["source"] = "nvml"
+            return out
+        if self._smi is None:
             return {"available": False}
-        self.proc.terminate()
+        self._smi.terminate()
         try:
-            self.proc.wait(timeout=5)
+            self._smi.wait(timeout=5)
         except subprocess.TimeoutExpired:
-            self.proc.kill()
-            self.proc.wait()
+            self._smi.kill()
+            self._smi.wait()
+        want = {b.upper().lstrip("0") for b in self.bus_ids}
         rows = []
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
         try:
-            with open(self.path) as f:
+            with open(self._path) as f:
                 for line in f:
                     parts = [p.strip() for p in line.split(",")]
-                    if len(parts) < 9:
+                    if len(parts) < 9 or (want and parts[0].upper().lstrip("0") not in want):
                         continue
-                    bus = parts[0].upper().lstrip("0")
-                    if self.bus_ids and bus not in self.bus_ids:
+                    try:
+                        rows.append((float(parts[1]), float(parts[2]), float(parts[3]),
+                                     {n for n, v in zip(names, parts[5:9]) if v.lower() == "active"}))
+                    except ValueError:
                         continue
-                    rows.append(parts)
         finally:
-            os.unlink(self.path)
-        if not rows:
-            return {"available": False}
-
-        def num(x):
-            try:
-                return float(x)
-            except ValueError:
-                return float("nan")
-
-        sm = [num(r[1]) for r in rows]
-        reasons = set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for r in rows:
-            for name, val in zip(names, r[5:9]):
-                if val.lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(num(r[2]) for r in rows),
-                "power_w_max": max(num(r[3]) for r in rows), "reasons": sorted(reasons),
-                "samples": len(rows)}
+            os.unlink(self._path)
+        out = _summarise(rows)
+        out["source"] = "nvidia-smi"
+        return out
 
 
 def clocks_ok(clocks: dict) -> bool:
