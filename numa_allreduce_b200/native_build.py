@@ -37,6 +37,9 @@ CORE_SOURCES = [
     "nab_capi.cpp",
 ]
 TORCH_SOURCES = ["nab_torch.cpp"]
+# Linked into libnab.so only: the allocation-free entry point, whose static
+# scratch array should not ride along in the torch extension.
+PLAIN_ONLY_SOURCES = ["nab_noalloc.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -144,16 +147,18 @@ def build(verbose: bool = False, jobs: int | None = None) -> dict[str, str]:
     with cf.ThreadPoolExecutor(max_workers=jobs) as ex:
         core_f = [ex.submit(_compile_one, CSRC / s, False, incs, defs, hdr, verbose) for s in CORE_SOURCES]
         torch_f = [ex.submit(_compile_one, CSRC / s, True, incs, defs, hdr, verbose) for s in TORCH_SOURCES]
+        plain_f = [ex.submit(_compile_one, CSRC / s, False, incs, defs, hdr, verbose) for s in PLAIN_ONLY_SOURCES]
         core = [f.result() for f in core_f]
         tobj = [f.result() for f in torch_f]
+        pobj = [f.result() for f in plain_f]
     cuda_lib = str(cuda / "lib64")
     _link(TORCH_LIB, core + tobj,
           [f"-L{torch_lib}", "-lc10", "-ltorch", "-ltorch_cpu", "-lc10_cuda", "-ltorch_cuda",
            f"-L{cuda_lib}", "-lcudart", f"-Wl,-rpath,{torch_lib}"], verbose)
-    _link(PLAIN_LIB, core,
+    _link(PLAIN_LIB, core + pobj,
           [f"-L{cuda_lib}", "-lcudart_static", "-ldl", "-lrt", "-lpthread"], verbose)
     # drop objects that no longer correspond to any current source
-    live = {o.name for o in core + tobj}
+    live = {o.name for o in core + tobj + pobj}
     for o in BUILD_DIR.glob("*.o"):
         if o.name not in live:
             o.unlink()
