@@ -133,7 +133,7 @@ def main():
             ref = None
     sizes = [int(v) for v in args.sizes.split(",")]
     if args.algos == "all":
-        algos = ["oneshot", "twoshot"] + (["nvls_oneshot", "nvls_twoshot"] if ar.has_nvls else []) + \
+        algos = ["oneshot", "twoshot", "twoshot_pipe"] + (["nvls_oneshot", "nvls_twoshot"] if ar.has_nvls else []) + \
                 (["hier"] if ar.hier_groups else [])
     elif args.algos == "auto":
         algos = ["auto"]

@@ -73,6 +73,10 @@ __global__ void __launch_bounds__(kThreads) k_copy(const __grid_constant__ ARPar
   for (; i < p.npacks; i += stride) st_plain(dst + i, ld_plain(src + i));
 }
 
+NAB_DINLINE void named_barrier(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // Loads in flight per thread: each phase issues all of its loads for U
 // consecutive packs before the first store, so a warp keeps ~8 independent
 // 16-byte requests outstanding (NVLink round trips are ~1-2 us).
@@ -269,6 +273,213 @@ __global__ void __launch_bounds__(kThreads, 1) k_twoshot(const __grid_constant__
   end_call(me, epoch);
 }
 
+// --------------------------------------------------------- twoshot pipe ----
+// Pipelined, warp-specialised two-shot with both phases done by stores (an
+// NVLink write carries its data in one packet; a read needs a request and a
+// response). Tiles of WS chunks flow through a ring of kPipeSlots slots per
+// CTA; every rank holds, per slot, WS reduce-scatter chunks and WS
+// all-gather chunks (one of each per source rank).
+//   pusher warps   store chunk j of tile k into owner j's slot, then release
+//                  the owner's per-CTA "pushed" flag (value: tile k + 1);
+//   reducer warps  acquire every peer's "pushed" flag, reduce the own chunk,
+//                  write it to the output and store it into every peer's
+//                  all-gather chunk, then release the peers' "reduced" flag;
+//   copier warps   acquire every owner's "reduced" flag, copy the gathered
+//                  chunks from the local slot into the output, free the slot.
+// Flags are monotonic per CTA and peer ((epoch << 20) | tile + 1), so one
+// flag covers every slot. A slot is reused by tile k + S only after this
+// rank's copiers finished tile k; every peer pushes tile k + S (and thus
+// overwrites this rank's chunks of tile k) only after its own copiers
+// finished tile k, which needed this rank's reduction of tile k.
+constexpr int kPushWarps = 4, kReduceWarps = 4, kPullWarps = 8;
+static_assert((kPushWarps + kReduceWarps + kPullWarps) * 32 == kThreads, "warp groups must fill the CTA");
+
+NAB_DINLINE bool wait_geq_cta(const uint64_t* addr, uint64_t target, const WaitCtx& w, uint32_t peer,
+                              uint32_t stage, volatile int* s_abort) {
+  uint64_t v = ld_acquire_sys(addr);
+  if (static_cast<int64_t>(v - target) >= 0) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    v = ld_acquire_sys(addr);
+    if (static_cast<int64_t>(v - target) >= 0) return true;
+    if ((it & 127u) == 0u) {
+      if (*s_abort || ld_volatile_u32(w.abort) != 0u) return false;
+      if (globaltimer_ns() - t0 > w.timeout_ns) {
+        record_failure(w, kErrTimeout, peer, stage, static_cast<uint32_t>(v));
+        return false;
+      }
+    }
+  }
+}
+
+template <typename T, int WS>
+__global__ void __launch_bounds__(kThreads, 1) k_twoshot_pipe(const __grid_constant__ ARParams p) {
+  constexpr int S = kPipeSlots;
+  constexpr int UP = Unroll<WS>::kPeer;
+  constexpr int UR = Unroll<WS>::kRed;
+  const RankView& me = p.v[blockIdx.y];
+  const int rank = me.rank;
+  const uint32_t epoch = begin_call(me);
+  const WaitCtx w = make_wait(p, me, epoch);
+  const int c = blockIdx.x;
+  const int C = gridDim.x;
+  const int chp = p.chunk_packs;
+  const int64_t tile = static_cast<int64_t>(WS) * chp;
+  const int64_t ntiles = (p.npacks + tile - 1) / tile;
+  const int64_t my_tiles = ntiles > c ? (ntiles - c + C - 1) / C : 0;
+  const int64_t cstride = p.L.pipe_chunk / 16;
+  const int64_t slot_packs = 2 * WS * cstride;  // [WS rs chunks][WS ag chunks]
+  auto ring = [&](int r) -> uint4* {
+    return reinterpret_cast<uint4*>(me.wsp[r] + p.L.pipe_off) + static_cast<int64_t>(c) * S * slot_packs;
+  };
+  const uint4* src = reinterpret_cast<const uint4*>(me.in);
+  uint4* dst = reinterpret_cast<uint4*>(me.out);
+  SignalPad* mypad = pad_of(me, rank);
+  int peers[WS - 1];
+  all_peers<WS>(rank, peers);
+
+  __shared__ int s_abort;
+  __shared__ int64_t s_done;  // tiles the pullers have finished (in order)
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    s_done = 0;
+  }
+  __syncthreads();
+  volatile int* abort_flag = &s_abort;
+  volatile int64_t* done = &s_done;
+  const int warp = threadIdx.x >> 5;
+  auto chunk_len = [&](int64_t tb, int owner) -> int {
+    return static_cast<int>(span_len(chp, p.npacks - (tb + static_cast<int64_t>(owner) * chp)));
+  };
+
+  if (warp < kPushWarps) {
+    // -------------------------------------------------------------- pushers
+    const int t = threadIdx.x, nt = kPushWarps * 32;
+    for (int64_t k = 0; k < my_tiles; ++k) {
+      const int slot = static_cast<int>(k % S);
+      if (t == 0 && k >= S) {
+        const uint64_t t0 = globaltimer_ns();
+        while (*done < k - S + 1 && !*abort_flag) {
+          if (globaltimer_ns() - t0 > w.timeout_ns) {
+            record_failure(w, kErrTimeout, 0xffffffffu, kStageRS, static_cast<uint32_t>(*done));
+            *abort_flag = 1;
+          }
+        }
+      }
+      named_barrier(1, nt);
+      if (*abort_flag) break;
+      const int64_t tb = (c + k * C) * tile;
+      int len[WS - 1];
+#pragma unroll
+      for (int q = 0; q < WS - 1; ++q) len[q] = chunk_len(tb, peers[q]);
+      for (int i0 = t; i0 < chp; i0 += nt * UP) {
+        uint4 x[UP][WS - 1];
+#pragma unroll
+        for (int u = 0; u < UP; ++u) {
+          const int i = i0 + u * nt;
+#pragma unroll
+          for (int q = 0; q < WS - 1; ++q)
+            if (i < len[q]) x[u][q] = ld_plain(src + tb + static_cast<int64_t>(peers[q]) * chp + i);
+        }
+#pragma unroll
+        for (int u = 0; u < UP; ++u) {
+          const int i = i0 + u * nt;
+#pragma unroll
+          for (int q = 0; q < WS - 1; ++q)
+            if (i < len[q]) st_plain(ring(peers[q]) + slot * slot_packs + rank * cstride + i, x[u][q]);
+        }
+      }
+      named_barrier(1, nt);
+      if (t < WS - 1) st_release_sys(&pad_at(me.wsp, peers[t])->flags[kFlagPipeRS].v[c][rank], make_seq(epoch, k + 1));
+    }
+  } else if (warp < kPushWarps + kReduceWarps) {
+    // ------------------------------------------------------------- reducers
+    const int t = threadIdx.x - kPushWarps * 32, nt = kReduceWarps * 32;
+    for (int64_t k = 0; k < my_tiles; ++k) {
+      const int slot = static_cast<int>(k % S);
+      bool ok = true;
+      if (t < WS - 1)
+        ok = wait_geq_cta(&mypad->flags[kFlagPipeRS].v[c][peers[t]], make_seq(epoch, k + 1), w, peers[t], kStageRS,
+                          abort_flag);
+      if (!ok) *abort_flag = 1;
+      named_barrier(2, nt);
+      if (*abort_flag) break;
+      const int64_t tb = (c + k * C) * tile;
+      const int64_t mb = tb + static_cast<int64_t>(rank) * chp;
+      const int mlen = chunk_len(tb, rank);
+      uint4* mine = ring(rank) + slot * slot_packs;
+      for (int i0 = t; i0 < mlen; i0 += nt * UR) {
+        uint4 x[UR][WS];
+#pragma unroll
+        for (int u = 0; u < UR; ++u) {
+          const int i = i0 + u * nt;
+          if (i < mlen) {
+#pragma unroll
+            for (int q = 0; q < WS; ++q) x[u][q] = (q == rank) ? ld_plain(src + mb + i) : ld_cg(mine + q * cstride + i);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < UR; ++u) {
+          const int i = i0 + u * nt;
+          if (i < mlen) {
+            Acc<T> a;
+            acc_set(a, x[u][0]);
+#pragma unroll
+            for (int q = 1; q < WS; ++q) acc_add(a, x[u][q]);
+            const uint4 y = acc_pack(a);
+            st_plain(dst + mb + i, y);
+#pragma unroll
+            for (int q = 0; q < WS - 1; ++q)
+              st_plain(ring(peers[q]) + slot * slot_packs + (WS + rank) * cstride + i, y);
+          }
+        }
+      }
+      named_barrier(2, nt);
+      if (t < WS - 1) st_release_sys(&pad_at(me.wsp, peers[t])->flags[kFlagPipeAG].v[c][rank], make_seq(epoch, k + 1));
+    }
+  } else {
+    // -------------------------------------------------------------- copiers
+    const int t = threadIdx.x - (kPushWarps + kReduceWarps) * 32, nt = kPullWarps * 32;
+    for (int64_t k = 0; k < my_tiles; ++k) {
+      const int slot = static_cast<int>(k % S);
+      bool ok = true;
+      if (t < WS - 1)
+        ok = wait_geq_cta(&mypad->flags[kFlagPipeAG].v[c][peers[t]], make_seq(epoch, k + 1), w, peers[t], kStageAG,
+                          abort_flag);
+      if (!ok) *abort_flag = 1;
+      named_barrier(3, nt);
+      if (*abort_flag) break;
+      const int64_t tb = (c + k * C) * tile;
+      int len[WS - 1];
+#pragma unroll
+      for (int q = 0; q < WS - 1; ++q) len[q] = chunk_len(tb, peers[q]);
+      for (int i0 = t; i0 < chp; i0 += nt * UP) {
+        uint4 x[UP][WS - 1];
+#pragma unroll
+        for (int u = 0; u < UP; ++u) {
+          const int i = i0 + u * nt;
+#pragma unroll
+          for (int q = 0; q < WS - 1; ++q)
+            if (i < len[q]) x[u][q] = ld_cg(ring(rank) + slot * slot_packs + (WS + peers[q]) * cstride + i);
+        }
+#pragma unroll
+        for (int u = 0; u < UP; ++u) {
+          const int i = i0 + u * nt;
+#pragma unroll
+          for (int q = 0; q < WS - 1; ++q)
+            if (i < len[q]) st_plain(dst + tb + static_cast<int64_t>(peers[q]) * chp + i, x[u][q]);
+        }
+      }
+      named_barrier(3, nt);
+      if (t == 0) {
+        __threadfence_block();
+        *done = k + 1;
+      }
+    }
+  }
+  end_call(me, epoch);
+}
+
 // ------------------------------------------------------------------ hier ----
 // Stage 1: reduce-scatter inside the group (chunk l -> local index l).
 // Stage 2: the owners of chunk l in all groups exchange their partial sums in
@@ -456,106 +667,185 @@ __global__ void __launch_bounds__(kThreads, 2) k_nvls_oneshot(const __grid_const
 }
 
 // ---------------------------------------------------------- NVLS twoshot ----
+// Pipelined and warp-specialised. Tiles of WS chunks (chunk j owned by rank j)
+// flow through a ring of kNvlsSlots slots in the CTA's part of the multicast
+// workspace:
+//   producer warps  copy tile k of the input into slot k % S (unicast address)
+//                   and arrive on the slot's phase-0 counter of every GPU;
+//   reducer warps   wait until every GPU copied tile k in, multimem.ld_reduce
+//                   their own chunk, multimem.st the result into the slot of
+//                   every GPU (and into their own output), arrive on phase 1;
+//   consumer warps  wait until every owner broadcast, copy the other chunks
+//                   out and hand the slot back to the producers.
+// Up to S tiles are in flight, so the local copies, the switch traffic and
+// the cross-GPU arrivals overlap. Counters are monotonic per slot: the n-th
+// use of a slot waits for WS * n arrivals. Every wait is bounded; a wait that
+// gives up sets a CTA-wide abort flag that every group checks.
+constexpr int kProdWarps = 4, kRedWarps = 8, kConsWarps = 4;
+static_assert((kProdWarps + kRedWarps + kConsWarps) * 32 == kThreads, "warp groups must fill the CTA");
+
+// One thread spins on a local counter (arrivals from every GPU) with a
+// deadline; also gives up when the CTA-wide abort flag is set.
+NAB_DINLINE bool pipe_wait(const uint32_t* ctr, uint32_t target, const WaitCtx& w, volatile int* s_abort,
+                           uint32_t stage) {
+  uint32_t v = ld_acquire_sys_u32(ctr);
+  if (static_cast<int32_t>(v - target) >= 0) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    v = ld_acquire_sys_u32(ctr);
+    if (static_cast<int32_t>(v - target) >= 0) return true;
+    if ((it & 127u) == 0u) {
+      if (*s_abort || ld_volatile_u32(w.abort) != 0u) return false;
+      if (globaltimer_ns() - t0 > w.timeout_ns) {
+        record_failure(w, kErrTimeout, 0xffffffffu, stage, v);
+        return false;
+      }
+    }
+  }
+}
+
 template <typename T, int WS>
 __global__ void __launch_bounds__(kThreads, 1) k_nvls_twoshot(const __grid_constant__ ARParams p) {
+  constexpr int S = kNvlsSlots;
   constexpr int U = 8;
-  constexpr int UL = 4;
+  constexpr int UL = 8;  // multimem.ld_reduce requests in flight per reducer thread
   const RankView& me = p.v[blockIdx.y];
   const int rank = me.rank;
   const uint32_t epoch = begin_call(me);
   const WaitCtx w = make_wait(p, me, epoch);
   const int c = blockIdx.x;
+  const int C = gridDim.x;
   const int chp = p.chunk_packs;
   const int64_t tile = static_cast<int64_t>(WS) * chp;
-  const int64_t stripe = tile * gridDim.x;
-  const int64_t slot_stride = p.L.chunk_max / 16;
-  const int64_t cta_off = p.L.mc_twoshot_off + static_cast<int64_t>(c) * WS * p.L.chunk_max;
-  uint4* uc = reinterpret_cast<uint4*>(me.uc + cta_off);
-  uint4* mc = reinterpret_cast<uint4*>(me.mc + cta_off);
+  const int64_t ntiles = (p.npacks + tile - 1) / tile;
+  const int64_t my_tiles = ntiles > c ? (ntiles - c + C - 1) / C : 0;
+  const int64_t cstride = p.L.nvls_chunk / 16;  // packs between chunks of a slot
+  const int64_t slot_packs = WS * cstride;
+  const int64_t cta_off = p.L.mc_twoshot_off + static_cast<int64_t>(c) * S * WS * p.L.nvls_chunk;
+  uint4* ucb = reinterpret_cast<uint4*>(me.uc + cta_off);
+  uint4* mcb = reinterpret_cast<uint4*>(me.mc + cta_off);
   NvlsPad* upad = reinterpret_cast<NvlsPad*>(me.uc);
   NvlsPad* mpad = reinterpret_cast<NvlsPad*>(me.mc);
   const uint4* src = reinterpret_cast<const uint4*>(me.in);
   uint4* dst = reinterpret_cast<uint4*>(me.out);
-  const int stride = blockDim.x;
+
   __shared__ uint32_t s_base;
-  __shared__ int s_ok;
-  if (threadIdx.x == 0) s_base = upad->rounds[c][0];
+  __shared__ int s_abort;
+  __shared__ int64_t s_done;  // tiles the consumers have finished (in order)
+  if (threadIdx.x == 0) {
+    s_base = upad->pipe_tiles[c];
+    s_abort = 0;
+    s_done = 0;
+  }
   __syncthreads();
   const uint32_t base = s_base;
-  bool ok = true;
-  for (int r = 0; r < p.rounds && ok; ++r) {
-    const int64_t tbase = r * stripe + c * tile;
-    const uint32_t target = (base + r + 1u) * WS;
-    const int tlen = static_cast<int>(span_len(tile, p.npacks - tbase));
-    // 1. copy the whole tile in; chunk j lives at uc + j * slot_stride
-    for (int i0 = threadIdx.x; i0 < tlen; i0 += stride * U) {
-      uint4 x[U];
-#pragma unroll
-      for (int u = 0; u < U; ++u)
-        if (i0 + u * stride < tlen) x[u] = ld_plain(src + tbase + i0 + u * stride);
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int i = i0 + u * stride;
-        if (i < tlen) st_plain(uc + (i / chp) * slot_stride + (i % chp), x[u]);
-      }
-    }
-    fence_proxy_alias();  // unicast stores before the multicast arrival
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      mm_red_add_release(&mpad->cnt[c][0][0], 1u);
-      s_ok = wait_geq_u32(&upad->cnt[c][0][0], target, w, kStageNvls1);
-    }
-    __syncthreads();
-    fence_proxy_alias();  // unicast acquire before multicast loads
-    ok = s_ok;
-    if (!ok) break;
-    // 2. reduce my chunk in the switch and broadcast the result
-    {
-      const int64_t mbase = tbase + static_cast<int64_t>(rank) * chp;
-      const int mlen = static_cast<int>(span_len(chp, p.npacks - mbase));
-      uint4* mchunk = mc + rank * slot_stride;
-      for (int i0 = threadIdx.x; i0 < mlen; i0 += stride * UL) {
-        uint4 y[UL];
-#pragma unroll
-        for (int u = 0; u < UL; ++u)
-          if (i0 + u * stride < mlen) y[u] = mm_ld_reduce<T>(mchunk + i0 + u * stride);
-#pragma unroll
-        for (int u = 0; u < UL; ++u) {
-          const int i = i0 + u * stride;
-          if (i < mlen) {
-            mm_st<T>(mchunk + i, y[u]);
-            st_plain(dst + mbase + i, y[u]);
+  volatile int* abort_flag = &s_abort;
+  volatile int64_t* done = &s_done;
+  const int warp = threadIdx.x >> 5;
+
+  if (warp < kProdWarps) {
+    // ------------------------------------------------------------ producers
+    const int t = threadIdx.x, nt = kProdWarps * 32;
+    for (int64_t k = 0; k < my_tiles; ++k) {
+      const uint32_t g = base + static_cast<uint32_t>(k);
+      const int slot = g % S;
+      if (t == 0 && k >= S) {  // the slot's previous tile must be consumed here
+        const uint64_t t0 = globaltimer_ns();
+        while (*done < k - S + 1 && !*abort_flag) {
+          if (globaltimer_ns() - t0 > w.timeout_ns) {
+            record_failure(w, kErrTimeout, 0xffffffffu, kStageNvls1, static_cast<uint32_t>(*done));
+            *abort_flag = 1;
           }
         }
       }
-    }
-    fence_proxy_alias();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      mm_red_add_release(&mpad->cnt[c][1][0], 1u);
-      s_ok = wait_geq_u32(&upad->cnt[c][1][0], target, w, kStageNvls2);
-    }
-    __syncthreads();
-    fence_proxy_alias();  // multicast stores of the peers before unicast loads
-    ok = s_ok;
-    if (!ok) break;
-    // 3. copy the other owners' results out of my local copy
-    for (int i0 = threadIdx.x; i0 < tlen; i0 += stride * U) {
-      uint4 x[U];
+      named_barrier(1, nt);
+      if (*abort_flag) break;
+      const int64_t tb = (c + k * C) * tile;
+      const int tlen = static_cast<int>(span_len(tile, p.npacks - tb));
+      uint4* us = ucb + slot * slot_packs;
+      for (int i0 = t; i0 < tlen; i0 += nt * U) {
+        uint4 x[U];
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int i = i0 + u * stride;
-        if (i < tlen && i / chp != rank) x[u] = ld_cg(uc + (i / chp) * slot_stride + (i % chp));
+        for (int u = 0; u < U; ++u)
+          if (i0 + u * nt < tlen) x[u] = ld_plain(src + tb + i0 + u * nt);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int i = i0 + u * nt;
+          if (i < tlen) st_plain(us + (i / chp) * cstride + (i % chp), x[u]);
+        }
       }
+      fence_proxy_alias();  // unicast stores before the multicast arrival
+      named_barrier(1, nt);
+      if (t == 0) mm_red_add_release(&mpad->pipe[c][slot][0][0], 1u);
+    }
+  } else if (warp < kProdWarps + kRedWarps) {
+    // ------------------------------------------------------------- reducers
+    const int t = threadIdx.x - kProdWarps * 32, nt = kRedWarps * 32;
+    for (int64_t k = 0; k < my_tiles; ++k) {
+      const uint32_t g = base + static_cast<uint32_t>(k);
+      const int slot = g % S;
+      const uint32_t target = WS * (g / S + 1u);
+      if (t == 0 && !pipe_wait(&upad->pipe[c][slot][0][0], target, w, abort_flag, kStageNvls1)) *abort_flag = 1;
+      named_barrier(2, nt);
+      if (*abort_flag) break;
+      fence_proxy_alias();  // unicast acquire before multicast loads
+      const int64_t mb = (c + k * C) * tile + static_cast<int64_t>(rank) * chp;
+      const int mlen = static_cast<int>(span_len(chp, p.npacks - mb));
+      uint4* mchunk = mcb + slot * slot_packs + rank * cstride;
+      for (int i0 = t; i0 < mlen; i0 += nt * UL) {
+        uint4 y[UL];
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int i = i0 + u * stride;
-        if (i < tlen && i / chp != rank) st_plain(dst + tbase + i, x[u]);
+        for (int u = 0; u < UL; ++u)
+          if (i0 + u * nt < mlen) y[u] = mm_ld_reduce<T>(mchunk + i0 + u * nt);
+#pragma unroll
+        for (int u = 0; u < UL; ++u) {
+          const int i = i0 + u * nt;
+          if (i < mlen) {
+            mm_st<T>(mchunk + i, y[u]);
+            st_plain(dst + mb + i, y[u]);
+          }
+        }
+      }
+      fence_proxy_alias();
+      named_barrier(2, nt);
+      if (t == 0) mm_red_add_release(&mpad->pipe[c][slot][1][0], 1u);
+    }
+  } else {
+    // ------------------------------------------------------------ consumers
+    const int t = threadIdx.x - (kProdWarps + kRedWarps) * 32, nt = kConsWarps * 32;
+    for (int64_t k = 0; k < my_tiles; ++k) {
+      const uint32_t g = base + static_cast<uint32_t>(k);
+      const int slot = g % S;
+      const uint32_t target = WS * (g / S + 1u);
+      if (t == 0 && !pipe_wait(&upad->pipe[c][slot][1][0], target, w, abort_flag, kStageNvls2)) *abort_flag = 1;
+      named_barrier(3, nt);
+      if (*abort_flag) break;
+      fence_proxy_alias();  // the owners' multicast stores before unicast loads
+      const int64_t tb = (c + k * C) * tile;
+      const int tlen = static_cast<int>(span_len(tile, p.npacks - tb));
+      const uint4* us = ucb + slot * slot_packs;
+      for (int i0 = t; i0 < tlen; i0 += nt * U) {
+        uint4 x[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int i = i0 + u * nt;
+          if (i < tlen && i / chp != rank) x[u] = ld_cg(us + (i / chp) * cstride + (i % chp));
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int i = i0 + u * nt;
+          if (i < tlen && i / chp != rank) st_plain(dst + tb + i, x[u]);
+        }
+      }
+      named_barrier(3, nt);
+      if (t == 0) {
+        __threadfence_block();
+        *done = k + 1;
       }
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0) upad->rounds[c][0] = base + p.rounds;
+  if (threadIdx.x == 0) upad->pipe_tiles[c] = base + static_cast<uint32_t>(my_tiles);
   end_call(me, epoch);
 }
 
@@ -565,6 +855,7 @@ cudaError_t launch_ws(int algo, const ARParams& p, dim3 grid, cudaStream_t s, bo
   switch (algo) {
     case kAlgoOneshot: fn = reinterpret_cast<void*>(&k_oneshot<T, WS>); break;
     case kAlgoTwoshot: fn = reinterpret_cast<void*>(&k_twoshot<T, WS>); break;
+    case kAlgoTwoshotPipe: fn = reinterpret_cast<void*>(&k_twoshot_pipe<T, WS>); break;
     case kAlgoHier: fn = reinterpret_cast<void*>(&k_hier<T>); break;
     case kAlgoOneshotPull: fn = reinterpret_cast<void*>(&k_oneshot_pull<T, WS>); break;
     case kAlgoNvlsOneshot: fn = reinterpret_cast<void*>(&k_nvls_oneshot<T, WS>); break;

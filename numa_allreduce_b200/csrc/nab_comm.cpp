@@ -77,6 +77,9 @@ Layout make_layout(int ws, const CommConfig& cfg) {
   L.hier_chunk = std::min<int64_t>(chunk, 32 << 10);
   L.hier_off = off;
   off += round_up(static_cast<int64_t>(L.hier_ctas) * (4 * ws + 2) * L.hier_chunk, kAlign);
+  L.pipe_off = off;
+  L.pipe_chunk = std::max<int64_t>(16 << 10, kPipeTileBytes / ws / 4096 * 4096);
+  off += round_up(static_cast<int64_t>(kPipeCtas) * kPipeSlots * 2 * ws * L.pipe_chunk, kAlign);
   L.fused_off = off;
   L.fused_bytes = round_up(cfg.fused_bytes, kAlign);
   off += 2 * ws * L.fused_bytes;
@@ -87,7 +90,8 @@ Layout make_layout(int ws, const CommConfig& cfg) {
   L.mc_oneshot_off = moff;
   moff += round_up(2 * cfg.oneshot_max, kAlign);
   L.mc_twoshot_off = moff;
-  moff += round_up(static_cast<int64_t>(cfg.max_ctas) * ws * chunk, kAlign);
+  L.nvls_chunk = std::max<int64_t>(16 << 10, kNvlsTileBytes / ws / 4096 * 4096);
+  moff += round_up(static_cast<int64_t>(kNvlsCtas) * kNvlsSlots * ws * L.nvls_chunk, kAlign);
   L.mc_bytes = moff;
   return L;
 }
@@ -243,8 +247,24 @@ LaunchPlan Communicator::plan(int64_t nbytes, int algo, bool registered) const {
       pl.grid = dim3(static_cast<unsigned>(b));
       break;
     }
+    case kAlgoTwoshotPipe:
+    case kAlgoNvlsTwoshot: {
+      // pipelined: tiles of ws chunks flow through each CTA's ring; small
+      // tiles for small messages so that they still spread over all CTAs
+      const bool nv = algo == kAlgoNvlsTwoshot;
+      const int64_t chunk_cap = (nv ? L_.nvls_chunk : L_.pipe_chunk) / 16;
+      const int kctas = nv ? kNvlsCtas : kPipeCtas;
+      const int64_t chp = std::min(chunk_cap, std::max<int64_t>(32, ceil_div_host(npacks, ws_ * kctas)));
+      const int64_t ntiles = ceil_div_host(npacks, ws_ * chp);
+      const int64_t C = clampv<int64_t>(ntiles, 1, kctas);
+      const int64_t per_cta = ceil_div_host(ntiles, C);
+      if (per_cta >= (int64_t(1) << 30)) throw std::invalid_argument("message too large");
+      pl.grid = dim3(static_cast<unsigned>(C));
+      pl.chunk_packs = static_cast<int>(chp);
+      pl.rounds = static_cast<int>(per_cta);
+      break;
+    }
     case kAlgoTwoshot:
-    case kAlgoNvlsTwoshot:
     case kAlgoHier: {
       const bool hier = algo == kAlgoHier;
       const int parts = hier ? gsize_ : ws_;
@@ -372,7 +392,9 @@ int emulate_allreduce(const std::vector<Communicator*>& comms, cudaStream_t s,
   if (pl.grid.x > cap) {
     const int64_t npacks = nbytes / 16;
     pl.grid.x = static_cast<unsigned>(cap);
-    if (pl.rounds > 0) {
+    // round-based protocols re-plan their tiling for the smaller grid; the
+    // pipelined one just gives each CTA more tiles
+    if (pl.rounds > 0 && (pl.algo == kAlgoTwoshot || pl.algo == kAlgoHier)) {
       ARParams tmp{};
       c0->fill_params(tmp, pl, nbytes);
       const int parts = (pl.algo == kAlgoHier) ? tmp.gsize : ws;

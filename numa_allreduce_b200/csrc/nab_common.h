@@ -29,7 +29,8 @@ enum Algo : int {
   kAlgoHier = 5,         // 3-stage: intra-group RS, inter-group AR, intra-group AG
   kAlgoOneshotPull = 6,  // registered inputs: read peers' buffers directly
   kAlgoCopy = 7,         // world size 1: out = in
-  kAlgoCount = 8,
+  kAlgoTwoshotPipe = 8,  // two-shot, warp-specialised and pipelined over a slot ring
+  kAlgoCount = 9,
 };
 
 // Error codes written into ErrorState::code by device code.
@@ -88,6 +89,8 @@ enum FlagKind : int {
   kFlagFusedAG,
   kFlagGemm,
   kFlagGemm2,
+  kFlagPipeRS,  // pipelined two-shot: tiles pushed to this rank, per CTA
+  kFlagPipeAG,  // pipelined two-shot: tiles reduced by the owner, per CTA
   kFlagCount,
 };
 
@@ -116,7 +119,22 @@ struct alignas(128) NvlsPad {
   // counters because each tracks its own expected count in `rounds`.
   uint32_t cnt[kMaxBlocks][3][8];
   uint32_t rounds[kMaxBlocks][2];  // [cta][0]=twoshot rounds, [cta][1]=oneshot calls
+  // Pipelined two-shot: arrival counters per [cta][ring slot][phase] (phase 0:
+  // tile copied in on every GPU, 1: tile reduced and broadcast by every owner)
+  // and the number of tiles each CTA index has pushed through its ring.
+  uint32_t pipe[kMaxBlocks][4][2][8];
+  uint32_t pipe_tiles[kMaxBlocks];
 };
+
+// Ring depth, CTA count and tile size of the pipelined P2P two-shot kernel.
+constexpr int kPipeSlots = 4;
+constexpr int kPipeCtas = 128;
+constexpr int64_t kPipeTileBytes = 256 << 10;
+
+// Ring depth and CTA count of the pipelined NVLS two-shot kernel.
+constexpr int kNvlsSlots = 4;
+constexpr int kNvlsCtas = 128;
+constexpr int64_t kNvlsTileBytes = 256 << 10;  // one ring slot: ws chunks
 
 constexpr uint64_t kSeqShift = 20;  // rounds per call < 2^20
 

@@ -30,6 +30,8 @@ struct Layout {
   int64_t oneshot_max;    // bytes per slot
   int64_t twoshot_off;    // [cta][ws rs slots + 1 result][chunk_max]
   int64_t hier_off;       // [cta][gsize rs + 2*ngroups*2 fp32 partials + 1 result][hier_chunk]
+  int64_t pipe_off;       // pipelined two-shot: [cta][ring slot][ws rs + ws ag chunks][pipe_chunk]
+  int64_t pipe_chunk;     // bytes per owner chunk in a ring slot
   int64_t fused_off;      // fused one-shot: [2 parities][ws slots][fused_bytes]
   int64_t fused_bytes;    // bytes per fused one-shot slot
   int64_t fused2_off;     // fused two-shot: [cta][ws rs rows + 1 result row][kFusedMaxHidden*2]
@@ -37,7 +39,8 @@ struct Layout {
   int64_t hier_chunk;     // bytes per owner chunk per round (hierarchical protocol)
   int64_t ws_bytes;       // total IPC workspace bytes
   int64_t mc_oneshot_off; // [2 parities][oneshot_max]
-  int64_t mc_twoshot_off; // [cta][ws chunks][chunk_max]
+  int64_t mc_twoshot_off; // [cta][ring slot][ws chunks][nvls_chunk]
+  int64_t nvls_chunk;     // bytes per owner chunk in a ring slot
   int64_t mc_bytes;
   int max_ctas;           // CTA slots the workspace was sized for
   int hier_ctas;          // CTA slots of the hierarchical region

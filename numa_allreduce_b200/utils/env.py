@@ -8,7 +8,7 @@ reads. Every variable below is actually read:
 =========================  ===================================================
 ``NAB_DISABLE``            ``1`` disables the custom path (callers fall back)
 ``NAB_ALGO``               force one protocol: ``oneshot``, ``twoshot``,
-                           ``nvls_oneshot``, ``nvls_twoshot``, ``hier``,
+                           ``twoshot_pipe``, ``nvls_oneshot``, ``nvls_twoshot``, ``hier``,
                            ``pull``, ``nccl`` or ``auto`` (default)
 ``NAB_MAX_SIZE``           largest message (bytes) the custom path takes
 ``NAB_TIMEOUT_NS``         bound of every device-side wait (default 5 s)
@@ -36,6 +36,7 @@ ALGO_IDS = {
     "hier": 5,
     "pull": 6,
     "copy": 7,
+    "twoshot_pipe": 8,
 }
 ALGO_NAMES = {v: k for k, v in ALGO_IDS.items()}
 NCCL = "nccl"

@@ -30,18 +30,18 @@ def _inputs(ws, numel, dtype, seed=0):
 def _schedule(algo, ws, groups=None):
     if algo == "oneshot":
         return HierSchedule.oneshot(ws)
-    if algo == "twoshot":
+    if algo in ("twoshot", "twoshot_pipe"):
         return HierSchedule.twoshot(ws)
     return HierSchedule.from_groups(groups)
 
 
 @pytest.mark.parametrize("ws", [2, 4, 8])
 @pytest.mark.parametrize("dtype", DTYPES)
-@pytest.mark.parametrize("algo", ["oneshot", "twoshot"])
+@pytest.mark.parametrize("algo", ["oneshot", "twoshot", "twoshot_pipe"])
 def test_flat_protocols_bit_exact(ws, dtype, algo):
     per_pack = 16 // torch.tensor([], dtype=dtype).element_size()
     sizes = [per_pack, per_pack * 3, 1024, 4096 * 7 + per_pack * 5, 65536]
-    if algo == "twoshot":
+    if algo != "oneshot":
         sizes.append(1 << 21)  # several rounds per CTA at the emulation grid
     with EmulatedGroup(ws, chunk_max=16 << 10) as g:
         for n in sizes:
@@ -84,14 +84,15 @@ def test_back_to_back_calls_and_protocol_switches():
     """Epochs and double buffers across many calls with changing grids."""
     ws = 4
     with EmulatedGroup(ws, chunk_max=16 << 10, groups=[[0, 1], [2, 3]]) as g:
-        algos = ["oneshot", "twoshot", "hier"]
+        algos = ["oneshot", "twoshot", "hier", "twoshot_pipe"]
         for i in range(300):
             n = [8, 1000 * 8, 50000 * 8, 8 * 3][i % 4]
-            algo = algos[i % 3]
+            algo = algos[i % 4]
             xs = _inputs(ws, n, torch.bfloat16, seed=i)
             outs = g.all_reduce(xs, algo=algo)
             if i % 25 == 0 or i > 290:
                 sched = {"oneshot": HierSchedule.oneshot(ws), "twoshot": HierSchedule.twoshot(ws),
+                         "twoshot_pipe": HierSchedule.twoshot(ws),
                          "hier": HierSchedule.from_groups([[0, 1], [2, 3]])}[algo]
                 ref = reference_allreduce([x.cpu() for x in xs], sched)
                 for r in range(ws):
@@ -103,7 +104,7 @@ def test_back_to_back_calls_and_protocol_switches():
 def test_in_place():
     ws = 4
     with EmulatedGroup(ws) as g:
-        for algo, n in [("oneshot", 4096), ("twoshot", 1 << 20)]:
+        for algo, n in [("oneshot", 4096), ("twoshot", 1 << 20), ("twoshot_pipe", 3 << 20)]:
             xs = _inputs(ws, n, torch.bfloat16, seed=3)
             ref = reference_allreduce([x.cpu() for x in xs], _schedule(algo, ws))
             g.all_reduce(xs, algo=algo, outs=xs)
@@ -111,7 +112,7 @@ def test_in_place():
                 assert torch.equal(xs[r].cpu(), ref)
 
 
-@pytest.mark.parametrize("algo", ["oneshot", "twoshot", "hier"])
+@pytest.mark.parametrize("algo", ["oneshot", "twoshot", "hier", "twoshot_pipe"])
 def test_absent_rank_times_out_and_recovers(algo):
     """A rank that never launches: the others' bounded waits give up, the
     error word names the stage, the context stays usable, and after reset()

@@ -11,9 +11,9 @@ from numa_allreduce_b200.utils.env import parse_groups, read_env
 def test_builtin_defaults():
     s = AlgoSelector(8, has_nvls=True)
     assert s.choose(4096) == "oneshot"
-    assert s.choose(64 << 20) == "nvls_twoshot"
+    assert s.choose(64 << 20) == "twoshot_pipe"
     s = AlgoSelector(8, has_nvls=False)
-    assert s.choose(64 << 20) == "twoshot"
+    assert s.choose(64 << 20) == "twoshot_pipe"
     assert AlgoSelector(1).choose(123) == "copy"
 
 
@@ -43,7 +43,7 @@ def test_table_round_trip(tmp_path):
     assert s.choose(1 << 28) == "nccl"
     assert s.choose(1 << 30) == "nccl"
     # other dtypes fall back to the built-in steps
-    assert s.choose(1 << 30, dtype="float32") == "twoshot"
+    assert s.choose(1 << 30, dtype="float32") == "twoshot_pipe"
 
 
 def test_table_custom_wins_at_top():
