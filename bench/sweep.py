@@ -54,6 +54,8 @@ def parse():
     p.add_argument("--write-table", default=None)
     p.add_argument("--max-oneshot", type=int, default=1 << 20)
     p.add_argument("--hier-groups", default=None, help="e.g. 0,1,2,3|4,5,6,7")
+    p.add_argument("--pipe-configs", default=None,
+                   help="extra pipelined two-shot configurations to time, e.g. 148x256,128x512 (CTAs x tile KiB)")
     return p.parse_args()
 
 
@@ -131,6 +133,13 @@ def main():
             if rank == 0:
                 print(f"reference unavailable: {e}", flush=True)
             ref = None
+    extra = []
+    if args.pipe_configs:
+        for spec in args.pipe_configs.split(","):
+            ctas, tile_kib = (int(v) for v in spec.split("x"))
+            extra.append((f"pipe_{ctas}x{tile_kib}",
+                          NumaAwareAllReduce(dist.group.WORLD, device=local, use_nvls=False, pipe_ctas=ctas,
+                                             pipe_tile=tile_kib << 10)))
     sizes = [int(v) for v in args.sizes.split(",")]
     if args.algos == "all":
         algos = ["oneshot", "twoshot", "twoshot_pipe"] + (["nvls_oneshot", "nvls_twoshot"] if ar.has_nvls else []) + \
@@ -159,6 +168,8 @@ def main():
                     continue
                 cands.append((algo if algo != "auto" else f"auto:{name}",
                               (lambda nm=name: ar.all_reduce(x, out=out, algo=nm)), True))
+            for label, comm in extra:
+                cands.append((label, (lambda c=comm: c.all_reduce(x, out=out, algo="twoshot_pipe")), True))
             if args.nccl:
                 y = x.clone()
                 cands.append(("nccl", lambda: dist.all_reduce(y), False))
@@ -201,6 +212,8 @@ def main():
                 json.dump(build_table(tab_rows), f, indent=1)
     torch.cuda.synchronize()
     ar.close()
+    for _, comm in extra:
+        comm.close()
     if ref is not None:
         ref.close()
     dist.destroy_process_group()

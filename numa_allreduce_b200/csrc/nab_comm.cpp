@@ -49,6 +49,20 @@ std::string cu_error_string(CUresult r) {
   return s ? std::string(s) : ("CUresult " + std::to_string(static_cast<int>(r)));
 }
 
+CommConfig config_from_list(const std::vector<int64_t>& v) {
+  CommConfig c;
+  auto at = [&](size_t i, int64_t d) { return i < v.size() ? v[i] : d; };
+  c.oneshot_max = at(0, c.oneshot_max);
+  c.chunk_max = at(1, c.chunk_max);
+  c.max_ctas = static_cast<int>(at(2, c.max_ctas));
+  c.oneshot_ctas = static_cast<int>(at(3, c.oneshot_ctas));
+  c.fused_bytes = at(4, c.fused_bytes);
+  c.timeout_ns = static_cast<uint64_t>(at(5, static_cast<int64_t>(c.timeout_ns)));
+  c.pipe_ctas = static_cast<int>(at(6, c.pipe_ctas));
+  c.pipe_tile = at(7, c.pipe_tile);
+  return c;
+}
+
 Layout make_layout(int ws, const CommConfig& cfg) {
   if (ws < 1 || ws > kMaxRanks) throw std::invalid_argument("world size must be in [1, 8]");
   if (cfg.max_ctas < 1 || cfg.max_ctas > kMaxBlocks || cfg.oneshot_ctas < 1 ||
@@ -57,6 +71,9 @@ Layout make_layout(int ws, const CommConfig& cfg) {
   if (cfg.chunk_max != 0 && (cfg.chunk_max < 16 * 512 || cfg.chunk_max % 16 != 0))
     throw std::invalid_argument("chunk_max must be 0 (auto) or a multiple of 16 and >= 8 KiB");
   if (cfg.oneshot_max % 16 != 0) throw std::invalid_argument("oneshot_max must be a multiple of 16");
+  if (cfg.pipe_ctas < 1 || cfg.pipe_ctas > kMaxBlocks) throw std::invalid_argument("pipe_ctas must be in [1, 160]");
+  if (cfg.pipe_tile < (64 << 10) || cfg.pipe_tile > (4 << 20))
+    throw std::invalid_argument("pipe_tile must be in [64 KiB, 4 MiB]");
   Layout L{};
   int64_t off = round_up(static_cast<int64_t>(sizeof(SignalPad)), kAlign);
   L.oneshot_off = off;
@@ -78,8 +95,9 @@ Layout make_layout(int ws, const CommConfig& cfg) {
   L.hier_off = off;
   off += round_up(static_cast<int64_t>(L.hier_ctas) * (4 * ws + 2) * L.hier_chunk, kAlign);
   L.pipe_off = off;
-  L.pipe_chunk = std::max<int64_t>(16 << 10, kPipeTileBytes / ws / 4096 * 4096);
-  off += round_up(static_cast<int64_t>(kPipeCtas) * kPipeSlots * 2 * ws * L.pipe_chunk, kAlign);
+  L.pipe_chunk = std::max<int64_t>(16 << 10, cfg.pipe_tile / ws / 4096 * 4096);
+  L.pipe_ctas = cfg.pipe_ctas;
+  off += round_up(static_cast<int64_t>(cfg.pipe_ctas) * kPipeSlots * 2 * ws * L.pipe_chunk, kAlign);
   L.fused_off = off;
   L.fused_bytes = round_up(cfg.fused_bytes, kAlign);
   off += 2 * ws * L.fused_bytes;
@@ -253,7 +271,7 @@ LaunchPlan Communicator::plan(int64_t nbytes, int algo, bool registered) const {
       // tiles for small messages so that they still spread over all CTAs
       const bool nv = algo == kAlgoNvlsTwoshot;
       const int64_t chunk_cap = (nv ? L_.nvls_chunk : L_.pipe_chunk) / 16;
-      const int kctas = nv ? kNvlsCtas : kPipeCtas;
+      const int kctas = nv ? kNvlsCtas : L_.pipe_ctas;
       const int64_t chp = std::min(chunk_cap, std::max<int64_t>(32, ceil_div_host(npacks, ws_ * kctas)));
       const int64_t ntiles = ceil_div_host(npacks, ws_ * chp);
       const int64_t C = clampv<int64_t>(ntiles, 1, kctas);

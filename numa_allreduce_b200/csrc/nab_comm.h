@@ -29,11 +29,17 @@ struct CommConfig {
   // Bytes per owner chunk per round of the two-shot protocols; 0 picks
   // 512 KiB / world size (a CTA moves ~512 KiB per round at any world size).
   int64_t chunk_max = 0;
-  int max_ctas = 128;             // CTAs of the tiled protocols
+  int max_ctas = 128;             // CTAs of the round-based tiled protocols
   int oneshot_ctas = 32;          // CTAs of the one-shot protocols
   int64_t fused_bytes = 512 << 10;  // fused one-shot slot (allreduce + norm)
   uint64_t timeout_ns = 5000000000ull;
+  int pipe_ctas = kPipeCtas;             // CTAs of the pipelined two-shot
+  int64_t pipe_tile = kPipeTileBytes;    // bytes per ring slot of the pipelined two-shot
 };
+
+// Config from a flat list: [oneshot_max, chunk_max, max_ctas, oneshot_ctas,
+// fused_bytes, timeout_ns, pipe_ctas, pipe_tile]; missing entries keep defaults.
+CommConfig config_from_list(const std::vector<int64_t>& v);
 
 // Computes where everything lives in the IPC and NVLS workspaces.
 Layout make_layout(int ws, const CommConfig& cfg);

@@ -44,6 +44,8 @@ struct Layout {
   int64_t mc_bytes;
   int max_ctas;           // CTA slots the workspace was sized for
   int hier_ctas;          // CTA slots of the hierarchical region
+  int pipe_ctas;          // CTA slots of the pipelined two-shot ring
+  int pad2_;
 };
 
 struct ARParams {

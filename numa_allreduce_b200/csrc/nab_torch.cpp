@@ -49,39 +49,22 @@ bool weak_contiguous(const at::Tensor& t) {
          (t.storage().nbytes() - t.storage_offset() * t.element_size() == t.numel() * t.element_size());
 }
 
-nab::CommConfig make_cfg(int64_t oneshot_max, int64_t chunk_max, int64_t max_ctas,
-                         int64_t oneshot_ctas, int64_t fused_bytes, int64_t timeout_ns) {
-  nab::CommConfig c;
-  c.oneshot_max = oneshot_max;
-  c.chunk_max = chunk_max;
-  c.max_ctas = static_cast<int>(max_ctas);
-  c.oneshot_ctas = static_cast<int>(oneshot_ctas);
-  c.fused_bytes = fused_bytes;
-  c.timeout_ns = static_cast<uint64_t>(timeout_ns);
-  return c;
-}
-
-std::vector<int64_t> layout(int64_t ws, int64_t oneshot_max, int64_t chunk_max, int64_t max_ctas,
-                            int64_t oneshot_ctas, int64_t fused_bytes) {
-  const nab::Layout L = nab::make_layout(
-      static_cast<int>(ws), make_cfg(oneshot_max, chunk_max, max_ctas, oneshot_ctas, fused_bytes, 1));
-  return {L.ws_bytes, L.mc_bytes, L.oneshot_off, L.twoshot_off, L.hier_off, L.fused_off};
+std::vector<int64_t> layout(int64_t ws, const std::vector<int64_t>& cfg) {
+  const nab::Layout L = nab::make_layout(static_cast<int>(ws), nab::config_from_list(cfg));
+  return {L.ws_bytes, L.mc_bytes, L.oneshot_off, L.twoshot_off, L.hier_off, L.fused_off, L.pipe_off};
 }
 
 int64_t meta_size() { return static_cast<int64_t>(sizeof(nab::SignalPad)); }
 
 fptr_t init(const std::vector<int64_t>& ws_ptrs, at::Tensor& rank_data, int64_t rank,
-            bool full_nvlink, int64_t oneshot_max, int64_t chunk_max, int64_t max_ctas,
-            int64_t oneshot_ctas, int64_t fused_bytes, int64_t timeout_ns) {
+            bool full_nvlink, const std::vector<int64_t>& cfg) {
   TORCH_CHECK(rank_data.is_cuda(), "rank_data must be a CUDA tensor");
   const at::cuda::OptionalCUDAGuard guard(rank_data.device());
   std::vector<char*> ptrs;
   for (int64_t p : ws_ptrs) ptrs.push_back(reinterpret_cast<char*>(p));
   auto* c = new Communicator(static_cast<int>(rank), static_cast<int>(ws_ptrs.size()), ptrs,
                              rank_data.data_ptr(), rank_data.numel() * rank_data.element_size(),
-                             make_cfg(oneshot_max, chunk_max, max_ctas, oneshot_ctas, fused_bytes,
-                                      timeout_ns),
-                             full_nvlink);
+                             nab::config_from_list(cfg), full_nvlink);
   return reinterpret_cast<fptr_t>(c);
 }
 
@@ -305,11 +288,9 @@ void emulate_fused_ar_rmsnorm(const std::vector<int64_t>& fas, const std::vector
 
 TORCH_LIBRARY(nab, m) {
   m.def("meta_size() -> int", &meta_size);
-  m.def("layout(int ws, int oneshot_max, int chunk_max, int max_ctas, int oneshot_ctas, int fused_bytes) -> int[]",
-        &layout);
-  m.def("init(int[] ws_ptrs, Tensor rank_data, int rank, bool full_nvlink, int oneshot_max, int chunk_max, "
-        "int max_ctas, int oneshot_ctas, int fused_bytes, int timeout_ns) -> int",
-        &init);
+  // cfg: [oneshot_max, chunk_max, max_ctas, oneshot_ctas, fused_bytes, timeout_ns, pipe_ctas, pipe_tile]
+  m.def("layout(int ws, int[] cfg) -> int[]", &layout);
+  m.def("init(int[] ws_ptrs, Tensor rank_data, int rank, bool full_nvlink, int[] cfg) -> int", &init);
   m.def("dispose(int fa) -> ()", &dispose);
   m.def("set_groups(int fa, int[] flat, int ngroups) -> ()", &set_groups);
   m.def("attach_nvls(int fa, int mc, int uc, int bytes) -> ()", &attach_nvls);

@@ -22,19 +22,19 @@ class EmulatedGroup:
     def __init__(self, world_size: int, device: torch.device | str = "cuda", *, oneshot_max: int = 1 << 20,
                  chunk_max: int = 0, max_ctas: int = 128, oneshot_ctas: int = 32,
                  fused_bytes: int = 512 << 10, timeout_ns: int = 2_000_000_000,
-                 groups: list[list[int]] | None = None):
+                 groups: list[list[int]] | None = None, pipe_ctas: int = 128, pipe_tile: int = 256 << 10):
         if not 2 <= world_size <= 8:
             raise ValueError("emulation needs 2..8 ranks")
         self.ops = _ext.load()
         self.world_size = world_size
         self.device = torch.device(device)
-        lay = self.ops.layout(world_size, oneshot_max, chunk_max, max_ctas, oneshot_ctas, fused_bytes)
+        cfg = [oneshot_max, chunk_max, max_ctas, oneshot_ctas, fused_bytes, timeout_ns, pipe_ctas, pipe_tile]
+        lay = self.ops.layout(world_size, cfg)
         self.workspaces = [torch.zeros(int(lay[0]), dtype=torch.uint8, device=self.device)
                            for _ in range(world_size)]
         self.rank_data = [torch.empty(1 << 16, dtype=torch.uint8, device=self.device) for _ in range(world_size)]
         ptrs = [w.data_ptr() for w in self.workspaces]
-        self.fas = [self.ops.init(ptrs, self.rank_data[r], r, True, oneshot_max, chunk_max, max_ctas,
-                                  oneshot_ctas, fused_bytes, timeout_ns) for r in range(world_size)]
+        self.fas = [self.ops.init(ptrs, self.rank_data[r], r, True, cfg) for r in range(world_size)]
         if groups:
             flat = [r for g in groups for r in g]
             for fa in self.fas:

@@ -81,7 +81,8 @@ class NumaAwareAllReduce:
 
     def __init__(self, group, device, max_size: int | None = None, enable_optimization: bool = True, *,
                  oneshot_max: int = 1 << 20, chunk_max: int = 0, max_ctas: int = 128,
-                 oneshot_ctas: int = 32, fused_bytes: int = 512 << 10,
+                 oneshot_ctas: int = 32, fused_bytes: int = 512 << 10, pipe_ctas: int | None = None,
+                 pipe_tile: int | None = None,
                  hier_groups: list[list[int]] | None = None, topology: NumaTopology | None = None,
                  use_nvls: bool | None = None, timeout_ns: int | None = None,
                  tuning_file: str | None = None):
@@ -141,17 +142,18 @@ class NumaAwareAllReduce:
             return
         self._fully_connected = self._check_full_nvlink()
 
-        self._cfg = dict(oneshot_max=oneshot_max, chunk_max=chunk_max, max_ctas=max_ctas,
-                         oneshot_ctas=oneshot_ctas, fused_bytes=fused_bytes)
-        lay = ops.layout(self.world_size, oneshot_max, chunk_max, max_ctas, oneshot_ctas, fused_bytes)
+        timeout = timeout_ns if timeout_ns is not None else self.env.timeout_ns
+        pipe_ctas = pipe_ctas if pipe_ctas is not None else self.env.pipe_ctas
+        pipe_tile = pipe_tile if pipe_tile is not None else self.env.pipe_tile
+        self._cfg = [oneshot_max, chunk_max, max_ctas, oneshot_ctas, fused_bytes, int(timeout), pipe_ctas,
+                     pipe_tile]
+        lay = ops.layout(self.world_size, self._cfg)
         self.workspace_bytes = int(lay[0])
         self.meta_ptrs = self._create_shared_buffer(self.workspace_bytes)
         self.buffer_ptrs = self.meta_ptrs
         self.rank_data = torch.empty(self.RANK_DATA_BYTES, dtype=torch.uint8, device=self.device)
-        timeout = timeout_ns if timeout_ns is not None else self.env.timeout_ns
         with torch.cuda.device(self.device):
-            self._ptr = ops.init(self.meta_ptrs, self.rank_data, self.rank, self._fully_connected,
-                                 oneshot_max, chunk_max, max_ctas, oneshot_ctas, fused_bytes, int(timeout))
+            self._ptr = ops.init(self.meta_ptrs, self.rank_data, self.rank, self._fully_connected, self._cfg)
         if self.hier_groups and self.enable_optimization:
             flat = [r for g in self.hier_groups for r in g]
             ops.set_groups(self._ptr, flat, len(self.hier_groups))

@@ -19,6 +19,8 @@ reads. Every variable below is actually read:
 ``NAB_SKIP_P2P_CHECK``     ``1`` trusts the driver for peer access
 ``NAB_CHECK``              ``1`` checks the device error word after every call
 ``NAB_NVTX``               ``1`` wraps calls in NVTX ranges
+``NAB_PIPE_CTAS``          CTAs of the pipelined two-shot (default 128)
+``NAB_PIPE_TILE``          bytes per ring slot of the pipelined two-shot
 =========================  ===================================================
 """
 
@@ -79,6 +81,8 @@ class EnvConfig:
     skip_p2p_check: bool = False
     check: bool = False
     nvtx: bool = False
+    pipe_ctas: int = 128
+    pipe_tile: int = 256 << 10
     extra: dict = field(default_factory=dict)
 
 
@@ -99,4 +103,6 @@ def read_env() -> EnvConfig:
         skip_p2p_check=_flag("NAB_SKIP_P2P_CHECK"),
         check=_flag("NAB_CHECK"),
         nvtx=_flag("NAB_NVTX"),
+        pipe_ctas=_int("NAB_PIPE_CTAS", 128),
+        pipe_tile=_int("NAB_PIPE_TILE", 256 << 10),
     )

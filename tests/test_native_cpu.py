@@ -12,14 +12,16 @@ def test_torch_ops_load_and_layout():
     ops = _ext.load()
     assert _ext.loaded_path().endswith("_C.so")
     assert ops.meta_size() > 0
-    ws_bytes, mc_bytes, one, two, hier, fused = ops.layout(8, 1 << 20, 64 << 10, 64, 32, 512 << 10)
-    assert 0 < one < two < hier < fused < ws_bytes
+    ws_bytes, mc_bytes, one, two, hier, fused, pipe = ops.layout(8, [1 << 20, 64 << 10, 64, 32, 512 << 10])
+    assert 0 < one < two < hier < pipe < fused < ws_bytes
     assert mc_bytes > 0
-    assert all(v % 4096 == 0 for v in (one, two, hier, fused))
+    assert all(v % 4096 == 0 for v in (one, two, hier, fused, pipe))
     with pytest.raises((RuntimeError, ValueError)):
-        ops.layout(9, 1 << 20, 64 << 10, 64, 32, 512 << 10)
+        ops.layout(9, [])
     with pytest.raises((RuntimeError, ValueError)):
-        ops.layout(8, 1 << 20, 100, 64, 32, 512 << 10)
+        ops.layout(8, [1 << 20, 100])
+    with pytest.raises((RuntimeError, ValueError)):
+        ops.layout(8, [1 << 20, 0, 128, 32, 512 << 10, 1, 128, 1000])  # pipe tile too small
 
 
 def test_c_abi_exports():
