@@ -268,6 +268,48 @@ __global__ void __launch_bounds__(kFThreads) k_fused_twoshot(const __grid_consta
   end_call(me.wsp, rank, epoch);
 }
 
+// Rank-order sum of the ws partial rows in this rank's one-shot slots, plus
+// the residual, then RMSNorm. The slot parity comes from the epoch of the
+// last completed call (the GEMM that filled the slots).
+template <int PPT>
+__global__ void __launch_bounds__(kFThreads) k_slots_rmsnorm(const char* base, const uint32_t* epoch_word,
+                                                             int64_t slot_off, int64_t slot_bytes, int ws,
+                                                             int splits, uint4* residual, const uint4* w,
+                                                             uint4* out, int T, int H, float eps) {
+  const int parity = ld_volatile_u32(epoch_word) & 1;
+  const int hp = H / 8;
+  auto slot = [&](int q) -> const char* {
+    return base + slot_off + (static_cast<int64_t>(parity) * ws + q) * slot_bytes;
+  };
+  for (int t = blockIdx.x; t < T; t += gridDim.x) {
+    float z[PPT][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < PPT; ++k) {
+      const int idx = threadIdx.x + k * kFThreads;
+      if (idx < hp) {
+        const int64_t o = static_cast<int64_t>(t) * hp + idx;
+        Acc<__nv_bfloat16> a;
+        if (splits == 1) {
+          acc_set(a, ld_cg(reinterpret_cast<const uint4*>(slot(0)) + o));
+          for (int q = 1; q < ws; ++q) acc_add(a, ld_cg(reinterpret_cast<const uint4*>(slot(q)) + o));
+        } else {
+          // fp32 partials: 8 values = 2 packs at element offset 8 * o
+          bool first = true;
+          for (int q = 0; q < ws; ++q)
+            for (int sp = 0; sp < splits; ++sp) {
+              const uint4* p4 = reinterpret_cast<const uint4*>(slot(q)) + (static_cast<int64_t>(sp) * T * hp + o) * 2;
+              acc_accum_f32(a, p4, first);
+              first = false;
+            }
+        }
+        ss += finish_pack(a, ld_plain(residual + o), residual + o, nullptr, z[k]);
+      }
+    }
+    norm_store<PPT>(z, ss, w, out + static_cast<int64_t>(t) * hp, hp, H, eps);
+  }
+}
+
 template <int WS, int PPT>
 void* pick_kernel(int algo) {
   return algo == kFusedOneshot ? reinterpret_cast<void*>(&k_fused_oneshot<WS, PPT>)
@@ -367,6 +409,31 @@ void check_ptrs(const void* a, const void* b, const void* c, const void* d) {
 }
 
 }  // namespace
+
+void slots_rmsnorm(Communicator& c, cudaStream_t s, void* residual, const void* weight, void* out, int64_t T,
+                   int64_t H, float eps, int splits) {
+  check_shape(T, H);
+  if (reinterpret_cast<uintptr_t>(residual) % 16 || reinterpret_cast<uintptr_t>(weight) % 16 ||
+      reinterpret_cast<uintptr_t>(out) % 16)
+    throw std::invalid_argument("slots rmsnorm: 16-byte alignment");
+  const Layout& L = c.layout();
+  const char* base = c.wsp(c.rank());
+  const uint32_t* epoch_word = &reinterpret_cast<const SignalPad*>(base)->epoch;
+  const int grid = static_cast<int>(std::min<int64_t>(T, 148 * 4));
+  auto* r4 = static_cast<uint4*>(residual);
+  const auto* w4 = static_cast<const uint4*>(weight);
+  auto* o4 = static_cast<uint4*>(out);
+  const int t = static_cast<int>(T), h = static_cast<int>(H), ws = c.world_size();
+  switch (ppt_for(H)) {
+    case 1: k_slots_rmsnorm<1><<<grid, kFThreads, 0, s>>>(base, epoch_word, L.fused_off, L.fused_bytes, ws, splits, r4, w4, o4, t, h, eps); break;
+    case 2: k_slots_rmsnorm<2><<<grid, kFThreads, 0, s>>>(base, epoch_word, L.fused_off, L.fused_bytes, ws, splits, r4, w4, o4, t, h, eps); break;
+    case 4: k_slots_rmsnorm<4><<<grid, kFThreads, 0, s>>>(base, epoch_word, L.fused_off, L.fused_bytes, ws, splits, r4, w4, o4, t, h, eps); break;
+    default: k_slots_rmsnorm<8><<<grid, kFThreads, 0, s>>>(base, epoch_word, L.fused_off, L.fused_bytes, ws, splits, r4, w4, o4, t, h, eps); break;
+  }
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string("slots rmsnorm launch failed: ") + cudaGetErrorString(e));
+  c.count_launch();
+}
 
 void rmsnorm_residual(cudaStream_t s, const void* inp, void* residual, const void* weight, void* out,
                       int64_t T, int64_t H, float eps) {

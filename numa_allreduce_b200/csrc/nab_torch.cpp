@@ -19,6 +19,8 @@
 
 #include "nab_comm.h"
 #include "nab_fused.h"
+#include "nab_gemm.h"
+#include "nab_llama.h"
 #include "nab_nvls.h"
 
 namespace {
@@ -284,6 +286,91 @@ void emulate_fused_ar_rmsnorm(const std::vector<int64_t>& fas, const std::vector
                                        static_cast<float>(eps), static_cast<int>(algo));
 }
 
+void check_gemm_operand(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.is_contiguous() && t.dim() == 2 && t.scalar_type() == at::kBFloat16, name,
+              " must be a contiguous 2-D bfloat16 CUDA tensor");
+}
+
+// y[T, N] = x[T, K] . wt[N, K]^T on the tcgen05 tensor cores.
+void gemm(const at::Tensor& x, const at::Tensor& wt, at::Tensor& y, const std::optional<at::Tensor>& ws,
+          int64_t splits) {
+  check_gemm_operand(x, "x");
+  check_gemm_operand(wt, "wt");
+  check_gemm_operand(y, "y");
+  TORCH_CHECK(x.size(1) == wt.size(1) && y.size(0) == x.size(0) && y.size(1) == wt.size(0), "GEMM shape mismatch");
+  const at::cuda::OptionalCUDAGuard guard(x.device());
+  auto stream = at::cuda::getCurrentCUDAStream().stream();
+  float* wsp = nullptr;
+  int64_t wsn = 0;
+  if (ws.has_value()) {
+    TORCH_CHECK(ws->is_cuda() && ws->scalar_type() == at::kFloat && ws->is_contiguous(), "split-K workspace must be fp32");
+    wsp = ws->data_ptr<float>();
+    wsn = ws->numel();
+  }
+  nab::gemm_bf16(stream, wt.data_ptr(), x.data_ptr(), y.data_ptr(), static_cast<int>(x.size(0)),
+                 static_cast<int>(wt.size(0)), static_cast<int>(x.size(1)), wsp, wsn, static_cast<int>(splits));
+}
+
+int64_t gemm_splits(int64_t T, int64_t N, int64_t K) {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return nab::gemm_splits_for(static_cast<int>(T), static_cast<int>(N), static_cast<int>(K), sms);
+}
+
+void gemm_ar_rmsnorm(fptr_t fa, const at::Tensor& x, const at::Tensor& wt, at::Tensor& residual,
+                     const at::Tensor& weight, at::Tensor& out, double eps, int64_t splits) {
+  check_gemm_operand(x, "x");
+  check_gemm_operand(wt, "wt");
+  check_gemm_operand(residual, "residual");
+  check_gemm_operand(out, "out");
+  TORCH_CHECK(x.size(1) == wt.size(1) && residual.size(0) == x.size(0) && residual.size(1) == wt.size(0) &&
+                  out.sizes() == residual.sizes(),
+              "GEMM+allreduce shape mismatch");
+  TORCH_CHECK(weight.is_contiguous() && weight.numel() == wt.size(0) && weight.scalar_type() == at::kBFloat16,
+              "norm weight must be [N] bfloat16");
+  const at::cuda::OptionalCUDAGuard guard(x.device());
+  auto stream = at::cuda::getCurrentCUDAStream().stream();
+  nab::gemm_allreduce_rmsnorm(*C(fa), stream, wt.data_ptr(), x.data_ptr(), residual.data_ptr(), weight.data_ptr(),
+                              out.data_ptr(), static_cast<int>(x.size(0)), static_cast<int>(wt.size(0)),
+                              static_cast<int>(x.size(1)), static_cast<float>(eps), static_cast<int>(splits));
+}
+
+void rope_append_op(const at::Tensor& qkv, const at::Tensor& cos_t, const at::Tensor& sin_t, const at::Tensor& pos,
+                    at::Tensor& q_out, at::Tensor& k_cache, at::Tensor& v_cache, int64_t Hq, int64_t Hkv) {
+  TORCH_CHECK(qkv.is_contiguous() && q_out.is_contiguous() && k_cache.is_contiguous() && v_cache.is_contiguous(),
+              "rope_append: contiguous tensors");
+  TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(3) == 128 && pos.scalar_type() == at::kInt, "rope_append: shapes");
+  TORCH_CHECK(cos_t.scalar_type() == at::kFloat && sin_t.scalar_type() == at::kFloat, "rope tables must be fp32");
+  const at::cuda::OptionalCUDAGuard guard(qkv.device());
+  nab::rope_append(at::cuda::getCurrentCUDAStream().stream(), qkv.data_ptr(), cos_t.data_ptr<float>(),
+                   sin_t.data_ptr<float>(), pos.data_ptr<int>(), q_out.data_ptr(), k_cache.data_ptr(),
+                   v_cache.data_ptr(), static_cast<int>(qkv.size(0)), static_cast<int>(Hq), static_cast<int>(Hkv),
+                   static_cast<int>(k_cache.size(2)));
+}
+
+void decode_attention_op(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
+                         const at::Tensor& pos, at::Tensor& part_ml, at::Tensor& part_o, at::Tensor& out,
+                         int64_t splits) {
+  TORCH_CHECK(q.dim() == 3 && q.size(2) == 128 && k_cache.dim() == 4, "decode_attention: shapes");
+  const int64_t B = q.size(0), Hq = q.size(1);
+  TORCH_CHECK(part_ml.numel() >= B * Hq * splits * 2 && part_o.numel() >= B * Hq * splits * 128,
+              "decode_attention: scratch too small");
+  const at::cuda::OptionalCUDAGuard guard(q.device());
+  nab::decode_attention(at::cuda::getCurrentCUDAStream().stream(), q.data_ptr(), k_cache.data_ptr(),
+                        v_cache.data_ptr(), pos.data_ptr<int>(), part_ml.data_ptr<float>(), part_o.data_ptr<float>(),
+                        out.data_ptr(), static_cast<int>(B), static_cast<int>(Hq),
+                        static_cast<int>(k_cache.size(1)), static_cast<int>(k_cache.size(2)),
+                        static_cast<int>(splits));
+}
+
+void silu_mul_op(const at::Tensor& gu, at::Tensor& out) {
+  TORCH_CHECK(gu.is_contiguous() && out.is_contiguous() && gu.dim() == 2 && gu.size(1) == 2 * out.size(1),
+              "silu_mul: shapes");
+  const at::cuda::OptionalCUDAGuard guard(gu.device());
+  nab::silu_mul(at::cuda::getCurrentCUDAStream().stream(), gu.data_ptr(), out.data_ptr(),
+                static_cast<int>(gu.size(0)), static_cast<int>(out.size(1)));
+}
+
 }  // namespace
 
 TORCH_LIBRARY(nab, m) {
@@ -334,6 +421,20 @@ TORCH_LIBRARY(nab, m) {
   m.def("emulate_fused_ar_rmsnorm(int[] fas, Tensor[] ins, Tensor(a!)[] residuals, Tensor[] weights, "
         "Tensor(b!)[] outs, float eps, int algo) -> ()");
   m.impl("emulate_fused_ar_rmsnorm", c10::kCUDA, &emulate_fused_ar_rmsnorm);
+  m.def("gemm(Tensor x, Tensor wt, Tensor(a!) y, Tensor? ws, int splits) -> ()");
+  m.impl("gemm", c10::kCUDA, &gemm);
+  m.def("gemm_splits(int T, int N, int K) -> int", &gemm_splits);
+  m.def("gemm_ar_rmsnorm(int fa, Tensor x, Tensor wt, Tensor(a!) residual, Tensor weight, Tensor(b!) out, "
+        "float eps, int splits=0) -> ()");
+  m.impl("gemm_ar_rmsnorm", c10::kCUDA, &gemm_ar_rmsnorm);
+  m.def("rope_append(Tensor qkv, Tensor cos, Tensor sin, Tensor pos, Tensor(a!) q_out, Tensor(b!) k_cache, "
+        "Tensor(c!) v_cache, int Hq, int Hkv) -> ()");
+  m.impl("rope_append", c10::kCUDA, &rope_append_op);
+  m.def("decode_attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor pos, Tensor(a!) part_ml, "
+        "Tensor(b!) part_o, Tensor(c!) out, int splits) -> ()");
+  m.impl("decode_attention", c10::kCUDA, &decode_attention_op);
+  m.def("silu_mul(Tensor gu, Tensor(a!) out) -> ()");
+  m.impl("silu_mul", c10::kCUDA, &silu_mul_op);
   m.def("rmsnorm_residual(Tensor inp, Tensor(a!) residual, Tensor weight, Tensor(b!) out, float eps) -> ()");
   m.impl("rmsnorm_residual", c10::kCUDA, &rmsnorm_residual);
 }

@@ -1,0 +1,214 @@
+"""Tensor-parallel Llama decoder for CUDA-graph decode.
+
+Llama-3 architecture (GQA attention with rotary embeddings, SwiGLU MLP,
+RMSNorm), sharded Megatron-style over the ranks: q/k/v and gate/up
+projections are column-parallel, o_proj and down_proj row-parallel, so each
+layer ends in two allreduces. Both are fused with the residual add and the
+next RMSNorm:
+
+* ``impl="fused"`` (this library): tcgen05 GEMMs; each row-parallel GEMM
+  stores its partial tiles into every rank's buffer over NVLink and a second
+  kernel adds them with the residual and applies the next RMSNorm (or, for
+  token counts where that is faster, the GEMM plus the fused allreduce +
+  residual + RMSNorm kernel);
+* ``impl="baseline"``: cuBLAS (``F.linear``) + NCCL ``all_reduce`` + residual
+  add + ``F.rms_norm``, the unfused stack.
+
+Attention (decode over a synthetic KV cache), RoPE and SwiGLU use this
+library's kernels in both variants so the comparison isolates the
+projections and the allreduces. Weights are random N(0, 0.02) (there is no
+checkpoint), the KV cache random N(0, 1); every buffer a step touches is
+static so the whole step is captured in one CUDA graph.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+from ..ops import _ext
+from ..ops.fused import fused_allreduce_rmsnorm, rmsnorm_residual
+from ..ops.gemm import gemm, gemm_allreduce_rmsnorm
+
+
+@dataclass
+class LlamaConfig:
+    hidden: int = 8192
+    layers: int = 80
+    heads: int = 64
+    kv_heads: int = 8
+    head_dim: int = 128
+    intermediate: int = 28672
+    vocab: int = 128256
+    rope_theta: float = 500000.0
+    eps: float = 1e-5
+
+    @classmethod
+    def llama3_70b(cls) -> "LlamaConfig":
+        return cls()
+
+    @classmethod
+    def llama3_8b(cls) -> "LlamaConfig":
+        return cls(hidden=4096, layers=32, heads=32, kv_heads=8, intermediate=14336)
+
+    @classmethod
+    def tiny(cls) -> "LlamaConfig":
+        return cls(hidden=1024, layers=2, heads=16, kv_heads=8, intermediate=2048, vocab=4096)
+
+
+def _round_up(x: int, a: int) -> int:
+    return (x + a - 1) // a * a
+
+
+class LlamaTPDecoder:
+    """One rank's shard of the model plus the static buffers of a decode step.
+
+    Args:
+        cfg: model shape.
+        comm: this rank's :class:`~numa_allreduce_b200.NumaAwareAllReduce`
+            (``None`` or world size 1 for a single GPU).
+        batch: sequences decoded per step.
+        context: tokens already in the (synthetic) KV cache; the step decodes
+            position ``context``.
+        impl: ``"fused"`` or ``"baseline"`` (see module docstring).
+    """
+
+    def __init__(self, cfg: LlamaConfig, comm, batch: int, context: int, impl: str = "fused", seed: int = 0,
+                 device: torch.device | str = "cuda", attn_splits: int | None = None):
+        if impl not in ("fused", "baseline"):
+            raise ValueError("impl must be 'fused' or 'baseline'")
+        self.cfg, self.comm, self.impl = cfg, comm, impl
+        self.device = torch.device(device)
+        self.world = comm.world_size if comm is not None and not comm.disabled else 1
+        self.rank = comm.rank if self.world > 1 else 0
+        if cfg.heads % self.world or cfg.intermediate % self.world:
+            raise ValueError("heads and intermediate size must divide by the world size")
+        self.ops = _ext.load()
+        W = self.world
+        D = cfg.head_dim
+        self.Hq = cfg.heads // W
+        self.Hkv = max(1, cfg.kv_heads // W)  # kv heads replicated when W > kv_heads
+        self.I = cfg.intermediate // W
+        self.B, self.ctx = batch, context
+        self.Lmax = _round_up(context + 1, 64)
+        H = cfg.hidden
+        g = torch.Generator(device=self.device).manual_seed(1234 + self.rank + 7919 * seed)
+
+        def w(rows, cols):
+            return (torch.randn(rows, cols, generator=g, device=self.device, dtype=torch.bfloat16) * 0.02)
+
+        qkv_rows = (self.Hq + 2 * self.Hkv) * D
+        self.layers = []
+        for _ in range(cfg.layers):
+            self.layers.append({
+                "wqkv": w(qkv_rows, H), "wo": w(H, self.Hq * D), "wgu": w(2 * self.I, H), "wd": w(H, self.I),
+                "in_norm": torch.ones(H, device=self.device, dtype=torch.bfloat16),
+                "post_norm": torch.ones(H, device=self.device, dtype=torch.bfloat16),
+                "k": torch.randn(batch, self.Hkv, self.Lmax, D, generator=g, device=self.device,
+                                 dtype=torch.bfloat16),
+                "v": torch.randn(batch, self.Hkv, self.Lmax, D, generator=g, device=self.device,
+                                 dtype=torch.bfloat16),
+            })
+        gv = torch.Generator(device=self.device).manual_seed(4321 + 7919 * seed)  # replicated tables
+        self.embed = torch.randn(cfg.vocab, H, generator=gv, device=self.device, dtype=torch.bfloat16) * 0.02
+        self.final_norm = torch.ones(H, device=self.device, dtype=torch.bfloat16)
+        self.v_local = _round_up((cfg.vocab + W - 1) // W, 128)
+        self.lm_head = w(self.v_local, H)
+        # rotary tables
+        inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, D, 2, device=self.device, dtype=torch.float64) / D))
+        ang = torch.arange(self.Lmax, device=self.device, dtype=torch.float64)[:, None] * inv[None, :]
+        self.cos, self.sin = ang.cos().float().contiguous(), ang.sin().float().contiguous()
+        # static step buffers
+        bf = dict(device=self.device, dtype=torch.bfloat16)
+        self.tokens = torch.zeros(batch, device=self.device, dtype=torch.long)
+        self.pos = torch.tensor([context], device=self.device, dtype=torch.int32)
+        self.h = torch.empty(batch, H, **bf)
+        self.x = torch.empty(batch, H, **bf)
+        self.qkv = torch.empty(batch, qkv_rows, **bf)
+        self.q = torch.empty(batch, self.Hq, D, **bf)
+        self.attn = torch.empty(batch, self.Hq * D, **bf)
+        self.gu = torch.empty(batch, 2 * self.I, **bf)
+        self.act = torch.empty(batch, self.I, **bf)
+        self.y = torch.empty(batch, H, **bf)
+        self.logits = torch.empty(batch, self.v_local, **bf)
+        self.splits = attn_splits or max(1, min(32, (context + 1) // 64))
+        self.part_ml = torch.empty(batch * self.Hq * self.splits * 2, device=self.device, dtype=torch.float32)
+        self.part_o = torch.empty(batch * self.Hq * self.splits * D, device=self.device, dtype=torch.float32)
+        self.gemm_splits = {}
+        self.next_tokens = torch.zeros(batch, device=self.device, dtype=torch.long)
+        self._gathered = torch.empty(W * batch * 2, device=self.device, dtype=torch.float32)
+
+    # --------------------------------------------------------------- pieces --
+    def _proj(self, x, wt, out):
+        if self.impl == "baseline":
+            out.copy_(F.linear(x, wt))
+        else:
+            gemm(x, wt, out=out)
+        return out
+
+    def _row_parallel_tail(self, inp, wt, norm_w):
+        """residual h += allreduce(inp @ wt.T); x = rmsnorm(h) * norm_w."""
+        eps = self.cfg.eps
+        if self.impl == "baseline":
+            y = F.linear(inp, wt)
+            if self.world > 1:
+                dist.all_reduce(y)
+            self.h.add_(y)
+            self.x.copy_(F.rms_norm(self.h, (self.cfg.hidden,), norm_w, eps))
+            return
+        if self.world == 1:
+            gemm(inp, wt, out=self.y)
+            rmsnorm_residual(self.y, self.h, norm_w, eps, out=self.x)
+        elif self.B <= 32:
+            gemm_allreduce_rmsnorm(self.comm, inp, wt, self.h, norm_w, eps, out=self.x)
+        else:
+            gemm(inp, wt, out=self.y)
+            fused_allreduce_rmsnorm(self.comm, self.y, self.h, norm_w, eps, out=self.x)
+
+    def step(self):
+        """One decode step (graph-capturable): tokens -> next tokens."""
+        cfg, ops = self.cfg, self.ops
+        torch.index_select(self.embed, 0, self.tokens, out=self.h)
+        self.x.copy_(F.rms_norm(self.h, (cfg.hidden,), self.layers[0]["in_norm"], cfg.eps))
+        for i, L in enumerate(self.layers):
+            self._proj(self.x, L["wqkv"], self.qkv)
+            ops.rope_append(self.qkv, self.cos, self.sin, self.pos, self.q, L["k"], L["v"], self.Hq, self.Hkv)
+            ops.decode_attention(self.q, L["k"], L["v"], self.pos, self.part_ml, self.part_o,
+                                 self.attn.view(self.B, self.Hq, cfg.head_dim), self.splits)
+            self._row_parallel_tail(self.attn, L["wo"], L["post_norm"])
+            self._proj(self.x, L["wgu"], self.gu)
+            ops.silu_mul(self.gu, self.act)
+            nxt = self.layers[i + 1]["in_norm"] if i + 1 < len(self.layers) else self.final_norm
+            self._row_parallel_tail(self.act, L["wd"], nxt)
+        self._proj(self.x, self.lm_head, self.logits)
+        val, idx = self.logits.float().max(dim=-1)
+        if self.world > 1:
+            mine = torch.stack([val, (idx + self.rank * self.v_local).float()], dim=-1).reshape(-1)
+            dist.all_gather_into_tensor(self._gathered, mine)
+            allv = self._gathered.view(self.world, self.B, 2)
+            best = allv[:, :, 0].argmax(dim=0)
+            self.next_tokens.copy_(allv[best, torch.arange(self.B, device=self.device), 1].long())
+        else:
+            self.next_tokens.copy_(idx)
+        return self.next_tokens
+
+    def reset_position(self):
+        self.pos.fill_(self.ctx)
+
+    def weight_bytes(self) -> int:
+        n = sum(t.numel() for L in self.layers for k, t in L.items() if k.startswith("w"))
+        return 2 * (n + self.lm_head.numel())
+
+
+def reference_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, length: int) -> torch.Tensor:
+    """fp32 GQA decode attention: q [B, Hq, D], k/v [B, Hkv, Lmax, D]."""
+    B, Hq, D = q.shape
+    Hkv = k.shape[1]
+    kk = k[:, :, :length].float().repeat_interleave(Hq // Hkv, dim=1)
+    vv = v[:, :, :length].float().repeat_interleave(Hq // Hkv, dim=1)
+    s = torch.einsum("bhd,bhld->bhl", q.float(), kk) / math.sqrt(D)
+    return torch.einsum("bhl,bhld->bhd", s.softmax(-1), vv)

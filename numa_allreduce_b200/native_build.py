@@ -32,6 +32,8 @@ PLAIN_LIB = PKG_DIR / "libnab.so"
 CORE_SOURCES = [
     "nab_allreduce.cu",
     "nab_fused.cu",
+    "nab_gemm_sm100.cu",
+    "nab_llama.cu",
     "nab_comm.cpp",
     "nab_nvls.cpp",
     "nab_capi.cpp",

@@ -1,0 +1,98 @@
+"""Decode-step kernels and the TP Llama decoder on one GPU, against PyTorch
+fp32 references."""
+
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from numa_allreduce_b200.models.llama_tp import LlamaConfig, LlamaTPDecoder, reference_attention
+from numa_allreduce_b200.ops import _ext
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,L", [(1, 8, 1, 1025), (4, 16, 8, 300), (2, 8, 2, 64)])
+def test_decode_attention(B, Hq, Hkv, L):
+    ops = _ext.load()
+    Lmax = ((L + 63) // 64) * 64
+    g = torch.Generator(device="cuda").manual_seed(0)
+    q = torch.randn(B, Hq, 128, generator=g, device="cuda").to(torch.bfloat16)
+    k = torch.randn(B, Hkv, Lmax, 128, generator=g, device="cuda").to(torch.bfloat16)
+    v = torch.randn(B, Hkv, Lmax, 128, generator=g, device="cuda").to(torch.bfloat16)
+    pos = torch.tensor([L - 1], device="cuda", dtype=torch.int32)
+    splits = max(1, L // 64)
+    ml = torch.empty(B * Hq * splits * 2, device="cuda")
+    po = torch.empty(B * Hq * splits * 128, device="cuda")
+    out = torch.empty(B, Hq, 128, device="cuda", dtype=torch.bfloat16)
+    ops.decode_attention(q, k, v, pos, ml, po, out, splits)
+    ref = reference_attention(q, k, v, L)
+    torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
+
+
+def test_rope_append():
+    ops = _ext.load()
+    B, Hq, Hkv, D, Lmax, pos = 2, 4, 2, 128, 64, 37
+    qkv = torch.randn(B, (Hq + 2 * Hkv) * D, device="cuda").to(torch.bfloat16)
+    inv = 1.0 / (500000.0 ** (torch.arange(0, D, 2, device="cuda", dtype=torch.float64) / D))
+    ang = torch.arange(Lmax, device="cuda", dtype=torch.float64)[:, None] * inv[None, :]
+    cos, sin = ang.cos().float().contiguous(), ang.sin().float().contiguous()
+    q = torch.empty(B, Hq, D, device="cuda", dtype=torch.bfloat16)
+    kc = torch.zeros(B, Hkv, Lmax, D, device="cuda", dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    ops.rope_append(qkv, cos, sin, torch.tensor([pos], device="cuda", dtype=torch.int32), q, kc, vc, Hq, Hkv)
+    x = qkv.float().view(B, Hq + 2 * Hkv, D)
+    c, s = cos[pos], sin[pos]
+
+    def rot(t):
+        a, b = t[..., :64], t[..., 64:]
+        return torch.cat([a * c - b * s, b * c + a * s], dim=-1)
+
+    torch.testing.assert_close(q.float(), rot(x[:, :Hq]), rtol=1e-2, atol=1e-2)
+    torch.testing.assert_close(kc[:, :, pos].float(), rot(x[:, Hq:Hq + Hkv]), rtol=1e-2, atol=1e-2)
+    assert torch.equal(vc[:, :, pos].float(), x[:, Hq + Hkv:].to(torch.bfloat16).float())
+
+
+def test_silu_mul():
+    ops = _ext.load()
+    gu = torch.randn(3, 2 * 512, device="cuda").to(torch.bfloat16)
+    out = torch.empty(3, 512, device="cuda", dtype=torch.bfloat16)
+    ops.silu_mul(gu, out)
+    ref = F.silu(gu[:, :512].float()) * gu[:, 512:].float()
+    torch.testing.assert_close(out.float(), ref, rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("B", [1, 4])
+def test_tiny_decoder_fused_matches_baseline(B):
+    cfg = LlamaConfig.tiny()
+    m = LlamaTPDecoder(cfg, None, batch=B, context=100)
+    m.tokens.copy_(torch.arange(B, device="cuda") + 5)
+    m.impl = "baseline"
+    m.step()
+    base_x, base_tok = m.x.float().clone(), m.next_tokens.clone()
+    m.impl = "fused"
+    m.step()
+    torch.cuda.synchronize()
+    rel = ((m.x.float() - base_x).norm() / base_x.norm()).item()
+    assert rel < 2e-2, rel
+    assert m.next_tokens.shape == base_tok.shape
+
+
+def test_tiny_decoder_cuda_graph_replay():
+    cfg = LlamaConfig.tiny()
+    m = LlamaTPDecoder(cfg, None, batch=2, context=50)
+    m.tokens.copy_(torch.tensor([1, 2], device="cuda"))
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        m.step()
+    torch.cuda.current_stream().wait_stream(s)
+    eager = m.x.float().clone()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        m.step()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.allclose(m.x.float(), eager, rtol=1e-3, atol=1e-3)
+    del g

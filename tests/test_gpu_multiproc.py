@@ -138,6 +138,55 @@ def _worker_graph(rank, ws, port, algo):
         dist.destroy_process_group()
 
 
+def _worker_gemm_ar(rank, ws, port):
+    """Fused row-parallel GEMM + allreduce + residual + RMSNorm (BASELINE
+    config 4 shapes) against a PyTorch fp32 reference of the same layer."""
+    from numa_allreduce_b200 import NumaAwareAllReduce
+    from numa_allreduce_b200.ops.gemm import gemm_allreduce_rmsnorm
+
+    _init(rank, ws, port)
+    errors = []
+    ar = None
+    try:
+        ar = NumaAwareAllReduce(dist.group.WORLD, device=rank, fused_bytes=8 << 20)
+        H, K = 4096, 1792
+        norm_w = torch.ones(H, device="cuda", dtype=torch.bfloat16)
+        for T in (1, 16, 128, 512):
+            g = torch.Generator(device="cuda").manual_seed(1000 * T + rank)
+            x = torch.randn(T, K, generator=g, device="cuda").to(torch.bfloat16)
+            wt = (torch.randn(H, K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+            gr = torch.Generator(device="cuda").manual_seed(77 + T)  # same residual on every rank
+            res = torch.randn(T, H, generator=gr, device="cuda").to(torch.bfloat16)
+            res0 = res.clone()
+            for rep in range(2):
+                res.copy_(res0)
+                out = gemm_allreduce_rmsnorm(ar, x, wt, res, norm_w, 1e-5)
+                torch.cuda.synchronize()
+            parts = (x.float() @ wt.float().t()).to(torch.bfloat16)  # each rank's partial, as the epilogue rounds it
+            gathered = [torch.empty_like(parts) for _ in range(ws)]
+            dist.all_gather(gathered, parts)
+            acc = gathered[0].float()
+            for p in gathered[1:]:
+                acc = acc + p.float()
+            z = (acc + res0.float()).to(torch.bfloat16).float()
+            ref = (z * torch.rsqrt(z.pow(2).mean(-1, keepdim=True) + 1e-5)).to(torch.bfloat16)
+            # the reference GEMM accumulates in another order: allow a bf16 ulp of the partials
+            if not torch.allclose(res.float(), z, rtol=1e-2, atol=6e-2):
+                errors.append(f"T={T}: residual mismatch {(res.float() - z).abs().max().item()}")
+            if not torch.allclose(out.float(), ref.float(), rtol=2e-2, atol=2e-2):
+                errors.append(f"T={T}: output mismatch {(out.float() - ref.float()).abs().max().item()}")
+        try:
+            ar.check()
+        except Exception as e:
+            errors.append(str(e))
+    finally:
+        torch.cuda.synchronize()
+        if ar is not None:
+            ar.close()
+        dist.destroy_process_group()
+    assert not errors, errors[:5]
+
+
 def _need(ws):
     if torch.cuda.device_count() < ws:
         pytest.skip(f"needs {ws} GPUs")
@@ -147,6 +196,12 @@ def _need(ws):
 def test_correctness_multiprocess(ws):
     _need(ws)
     mp.spawn(_worker_correctness, args=(ws, free_port()), nprocs=ws, join=True)
+
+
+@pytest.mark.parametrize("ws", [2, 8])
+def test_gemm_allreduce_rmsnorm(ws):
+    _need(ws)
+    mp.spawn(_worker_gemm_ar, args=(ws, free_port()), nprocs=ws, join=True)
 
 
 @pytest.mark.parametrize("algo", ["auto", "pull"])
