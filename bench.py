@@ -148,7 +148,9 @@ def timed_sweep(arm, xs, outs, sizes, steps, warmup, rank, bus_ids):
     ev = {s: [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
               for _ in range(steps)] for s in sizes}
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    sampler = ClockSampler(bus_ids).start() if rank == 0 else None
+    sampler = ClockSampler(bus_ids).start() if rank == 0 and os.environ.get("NAB_BENCH_NO_CLOCKS") != "1" else None
+    dist.barrier()
+    torch.cuda.synchronize()
     l0 = arm.launches()
     start.record()
     for k in range(steps):

@@ -68,116 +68,113 @@ def _summarise(rows: list[tuple[float, float, float, set]]) -> dict:
             "power_w_max": round(max(r[2] for r in rows), 1), "reasons": sorted(reasons), "samples": len(rows)}
 
 
+_SAMPLER_SRC = r"""
+import sys, time, pynvml
+out, interval, ids = sys.argv[1], float(sys.argv[2]), sys.argv[3:]
+pynvml.nvmlInit()
+hs = [pynvml.nvmlDeviceGetHandleByPciBusId(b) for b in ids] if ids else \
+     [pynvml.nvmlDeviceGetHandleByIndex(i) for i in range(pynvml.nvmlDeviceGetCount())]
+get = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+with open(out, "w", buffering=1) as f:
+    print("ready", file=f)
+    while True:
+        for h in hs:
+            f.write("%d,%d,%.1f,%d\n" % (pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
+                    pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM),
+                    pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0, int(get(h))))
+        time.sleep(interval)
+"""
+
+
 class ClockSampler:
     """Samples SM clocks, power and throttle reasons while active.
 
-    Polls NVML from a background thread every ``interval_ms`` (a few ms, so a
-    short timed region still gets samples); without NVML it runs
-    ``nvidia-smi --loop-ms``. ``stop()`` returns ``{"sm_mhz": median,
+    Runs in a separate process (NVML, every ``interval_ms``; ``nvidia-smi``
+    if NVML is missing), so the sampling never competes with the benchmark's
+    own kernel launches. ``stop()`` returns ``{"sm_mhz": median,
     "sm_max_mhz", "power_w_max", "reasons": [...], "samples"}`` over the GPUs
     whose PCI bus ids were given. It only reads; nothing on the GPU changes.
     """
 
-    def __init__(self, bus_ids: list[str] | None = None, interval_ms: int = 5):
+    def __init__(self, bus_ids: list[str] | None = None, interval_ms: int = 10):
         self.bus_ids = list(bus_ids) if bus_ids else []
         self.interval_ms = interval_ms
-        self._thread = None
-        self._stop = None
-        self._rows: list = []
-        self._smi = None
-        self._path = None
+        self.proc = None
+        self.path = None
+        self.kind = None
 
-    def start(self) -> "ClockSampler":
-        try:
-            import threading
+    def start(self, wait_s: float = 5.0) -> "ClockSampler":
+        import sys
+        import time
 
-            import pynvml
-
-            pynvml.nvmlInit()
-            if self.bus_ids:
-                handles = [pynvml.nvmlDeviceGetHandleByPciBusId(b) for b in self.bus_ids]
-            else:
-                handles = [pynvml.nvmlDeviceGetHandleByIndex(i) for i in range(pynvml.nvmlDeviceGetCount())]
-            get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
-                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
-            self._stop = threading.Event()
-
-            def sample():
-                for h in handles:
-                    sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
-                    mx = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
-                    pw = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
-                    bits = int(get_reasons(h))
-                    self._rows.append((sm, mx, pw, {k for k, b in _NVML_REASONS.items() if bits & b}))
-
-            def loop():
-                while not self._stop.is_set():
-                    try:
-                        sample()
-                    except Exception:
-                        return
-                    self._stop.wait(self.interval_ms / 1000.0)
-                try:
-                    sample()
-                except Exception:
-                    pass
-
-            sample()
-            self._thread = threading.Thread(target=loop, daemon=True)
-            self._thread.start()
-            return self
-        except Exception:
-            self._thread = None
-        fd, self._path = tempfile.mkstemp(prefix="nab_clocks_", suffix=".csv")
+        fd, self.path = tempfile.mkstemp(prefix="nab_clocks_", suffix=".csv")
         os.close(fd)
         try:
-            self._smi = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={CLOCK_FIELDS}", "--format=csv,noheader,nounits",
-                 f"--loop-ms={max(100, self.interval_ms)}", f"--filename={self._path}"],
-                stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
-        except (OSError, ValueError):
-            self._smi = None
+            import pynvml  # noqa: F401
+
+            self.proc = subprocess.Popen([sys.executable, "-c", _SAMPLER_SRC, self.path,
+                                          str(self.interval_ms / 1000.0), *self.bus_ids],
+                                         stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+            self.kind = "nvml"
+        except (ImportError, OSError):
+            try:
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", f"--query-gpu={CLOCK_FIELDS}", "--format=csv,noheader,nounits",
+                     f"--loop-ms={max(100, self.interval_ms)}", f"--filename={self.path}"],
+                    stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+                self.kind = "nvidia-smi"
+            except OSError:
+                self.proc = None
+        # wait until the sampler is producing, so the timed region is covered
+        t0 = time.time()
+        while self.proc is not None and time.time() - t0 < wait_s:
+            if self.proc.poll() is not None:
+                break
+            try:
+                if os.path.getsize(self.path) > 0:
+                    break
+            except OSError:
+                pass
+            time.sleep(0.01)
         return self
 
     def stop(self) -> dict:
-        if self._thread is not None:
-            self._stop.set()
-            self._thread.join(timeout=5)
-            try:
-                import pynvml
-
-                pynvml.nvmlShutdown()
-            except Exception:
-                pass
-            out = _summarise(self._rows)
-            out["source"] = "nvml"
-            return out
-        if self._smi is None:
+        if self.proc is None:
             return {"available": False}
-        self._smi.terminate()
+        self.proc.terminate()
         try:
-            self._smi.wait(timeout=5)
+            self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
-            self._smi.kill()
-            self._smi.wait()
-        want = {b.upper().lstrip("0") for b in self.bus_ids}
+            self.proc.kill()
+            self.proc.wait()
         rows = []
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
         try:
-            with open(self._path) as f:
-                for line in f:
-                    parts = [p.strip() for p in line.split(",")]
-                    if len(parts) < 9 or (want and parts[0].upper().lstrip("0") not in want):
-                        continue
-                    try:
-                        rows.append((float(parts[1]), float(parts[2]), float(parts[3]),
-                                     {n for n, v in zip(names, parts[5:9]) if v.lower() == "active"}))
-                    except ValueError:
-                        continue
+            with open(self.path) as f:
+                lines = f.read().splitlines()
         finally:
-            os.unlink(self._path)
+            os.unlink(self.path)
+        if self.kind == "nvml":
+            for line in lines:
+                parts = line.split(",")
+                if len(parts) != 4:
+                    continue
+                bits = int(parts[3])
+                rows.append((float(parts[0]), float(parts[1]), float(parts[2]),
+                             {k for k, b in _NVML_REASONS.items() if bits & b}))
+        else:
+            want = {b.upper().lstrip("0") for b in self.bus_ids}
+            names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+            for line in lines:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9 or (want and parts[0].upper().lstrip("0") not in want):
+                    continue
+                try:
+                    rows.append((float(parts[1]), float(parts[2]), float(parts[3]),
+                                 {n for n, v in zip(names, parts[5:9]) if v.lower() == "active"}))
+                except ValueError:
+                    continue
         out = _summarise(rows)
-        out["source"] = "nvidia-smi"
+        out["source"] = self.kind
         return out
 
 
