@@ -15,6 +15,8 @@ namespace nab {
 constexpr int kMaxRanks = 8;
 // Flag slots per protocol: one per CTA index. 160 >= 148 SMs of a B200.
 constexpr int kMaxBlocks = 160;
+// Output tiles (128 features x up to 256 tokens) of one GEMM + allreduce call.
+constexpr int kGemmMaxTiles = 1024;
 
 enum DType : int { kF32 = 0, kF16 = 1, kBF16 = 2 };
 
@@ -87,8 +89,6 @@ enum FlagKind : int {
   kFlagFused,
   kFlagFusedRS,
   kFlagFusedAG,
-  kFlagGemm,
-  kFlagGemm2,
   kFlagPipeRS,  // pipelined two-shot: tiles pushed to this rank, per CTA
   kFlagPipeAG,  // pipelined two-shot: tiles reduced by the owner, per CTA
   kFlagCount,
@@ -108,6 +108,9 @@ struct alignas(128) SignalPad {
   // Rounds each CTA index has completed in the hierarchical protocol; the
   // same on every rank. Its parity picks the double-buffered stage-2 slots.
   alignas(128) uint32_t hier_rounds[kMaxBlocks];
+  // GEMM + allreduce: rank r raises [tile][r] on every rank once its output
+  // tile is in every rank's slot.
+  alignas(128) uint64_t gemm_flags[kGemmMaxTiles][kMaxRanks];
 };
 
 // Header of the NVLS (multicast) workspace. The counters are incremented on

@@ -167,6 +167,11 @@ NAB_DINLINE uint32_t ld_volatile_u32(const uint32_t* p) {
 NAB_DINLINE void st_volatile_u32(uint32_t* p, uint32_t v) {
   asm volatile("st.volatile.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+// Programmatic dependent launch: lets a kernel launched after this one with
+// programmatic stream serialization begin scheduling now (it waits for this
+// grid's completion before it reads anything this grid writes).
+NAB_DINLINE void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 NAB_DINLINE uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -115,6 +115,7 @@ template <int PPT>
 __global__ void __launch_bounds__(kFThreads) k_rmsnorm(const uint4* __restrict__ in, uint4* residual,
                                                        const uint4* __restrict__ w, uint4* out, int T,
                                                        int H, float eps) {
+  pdl_trigger();
   const int hp = H / 8;
   for (int t = blockIdx.x; t < T; t += gridDim.x) {
     float z[PPT][8];
@@ -135,6 +136,7 @@ __global__ void __launch_bounds__(kFThreads) k_rmsnorm(const uint4* __restrict__
 
 template <int WS, int PPT>
 __global__ void __launch_bounds__(kFThreads) k_fused_oneshot(const __grid_constant__ FusedParams p) {
+  pdl_trigger();
   const FusedView& me = p.v[blockIdx.y];
   const int rank = me.rank;
   const uint32_t epoch = begin_call(me.wsp, rank);
@@ -189,6 +191,7 @@ __global__ void __launch_bounds__(kFThreads) k_fused_oneshot(const __grid_consta
 
 template <int WS, int PPT>
 __global__ void __launch_bounds__(kFThreads) k_fused_twoshot(const __grid_constant__ FusedParams p) {
+  pdl_trigger();
   const FusedView& me = p.v[blockIdx.y];
   const int rank = me.rank;
   const uint32_t epoch = begin_call(me.wsp, rank);
@@ -272,16 +275,33 @@ __global__ void __launch_bounds__(kFThreads) k_fused_twoshot(const __grid_consta
 // the residual, then RMSNorm. The slot parity comes from the epoch of the
 // last completed call (the GEMM that filled the slots).
 template <int PPT>
-__global__ void __launch_bounds__(kFThreads) k_slots_rmsnorm(const char* base, const uint32_t* epoch_word,
-                                                             int64_t slot_off, int64_t slot_bytes, int ws,
-                                                             int splits, uint4* residual, const uint4* w,
-                                                             uint4* out, int T, int H, float eps) {
-  const int parity = ld_volatile_u32(epoch_word) & 1;
+__global__ void __launch_bounds__(kFThreads) k_slots_rmsnorm(const char* base, int64_t slot_off, int64_t slot_bytes,
+                                                             int ws, int tile_tokens, int m_tiles, WaitCtx w,
+                                                             uint4* residual, const uint4* wgt, uint4* out, int T,
+                                                             int H, float eps) {
+  pdl_trigger();
+  const SignalPad* pad = reinterpret_cast<const SignalPad*>(base);
+  const uint32_t epoch = ld_volatile_u32(&pad->epoch);
+  const int parity = epoch & 1;
+  const uint64_t seq = make_seq(epoch, 0);
+  w.epoch = epoch;
   const int hp = H / 8;
   auto slot = [&](int q) -> const char* {
     return base + slot_off + (static_cast<int64_t>(parity) * ws + q) * slot_bytes;
   };
+  int ready_tile = -1;
   for (int t = blockIdx.x; t < T; t += gridDim.x) {
+    if (tile_tokens > 0 && t / tile_tokens != ready_tile) {
+      // every rank's output tiles covering row t must have landed here
+      ready_tile = t / tile_tokens;
+      bool ok = true;
+      for (int i = threadIdx.x; i < m_tiles * ws; i += kFThreads) {
+        const int m = i / ws, q = i % ws;
+        ok &= wait_geq(&pad->gemm_flags[ready_tile * m_tiles + m][q], seq, w, static_cast<uint32_t>(q),
+                       kStageGemmAR);
+      }
+      if (!__syncthreads_and(ok)) return;
+    }
     float z[PPT][8];
     float ss = 0.f;
 #pragma unroll
@@ -289,24 +309,19 @@ __global__ void __launch_bounds__(kFThreads) k_slots_rmsnorm(const char* base, c
       const int idx = threadIdx.x + k * kFThreads;
       if (idx < hp) {
         const int64_t o = static_cast<int64_t>(t) * hp + idx;
+        uint4 v[kMaxRanks];
+#pragma unroll
+        for (int q = 0; q < kMaxRanks; ++q)
+          if (q < ws) v[q] = ld_cg(reinterpret_cast<const uint4*>(slot(q)) + o);
         Acc<__nv_bfloat16> a;
-        if (splits == 1) {
-          acc_set(a, ld_cg(reinterpret_cast<const uint4*>(slot(0)) + o));
-          for (int q = 1; q < ws; ++q) acc_add(a, ld_cg(reinterpret_cast<const uint4*>(slot(q)) + o));
-        } else {
-          // fp32 partials: 8 values = 2 packs at element offset 8 * o
-          bool first = true;
-          for (int q = 0; q < ws; ++q)
-            for (int sp = 0; sp < splits; ++sp) {
-              const uint4* p4 = reinterpret_cast<const uint4*>(slot(q)) + (static_cast<int64_t>(sp) * T * hp + o) * 2;
-              acc_accum_f32(a, p4, first);
-              first = false;
-            }
-        }
+        acc_set(a, v[0]);
+#pragma unroll
+        for (int q = 1; q < kMaxRanks; ++q)
+          if (q < ws) acc_add(a, v[q]);
         ss += finish_pack(a, ld_plain(residual + o), residual + o, nullptr, z[k]);
       }
     }
-    norm_store<PPT>(z, ss, w, out + static_cast<int64_t>(t) * hp, hp, H, eps);
+    norm_store<PPT>(z, ss, wgt, out + static_cast<int64_t>(t) * hp, hp, H, eps);
   }
 }
 
@@ -411,24 +426,31 @@ void check_ptrs(const void* a, const void* b, const void* c, const void* d) {
 }  // namespace
 
 void slots_rmsnorm(Communicator& c, cudaStream_t s, void* residual, const void* weight, void* out, int64_t T,
-                   int64_t H, float eps, int splits) {
+                   int64_t H, float eps, int tile_tokens) {
   check_shape(T, H);
   if (reinterpret_cast<uintptr_t>(residual) % 16 || reinterpret_cast<uintptr_t>(weight) % 16 ||
       reinterpret_cast<uintptr_t>(out) % 16)
     throw std::invalid_argument("slots rmsnorm: 16-byte alignment");
+  if (H % 128 != 0 && tile_tokens > 0) throw std::invalid_argument("slots rmsnorm: H must be a multiple of 128");
   const Layout& L = c.layout();
   const char* base = c.wsp(c.rank());
-  const uint32_t* epoch_word = &reinterpret_cast<const SignalPad*>(base)->epoch;
+  WaitCtx w{};
+  w.err = c.err_dev();
+  w.err_host = c.err_host();
+  w.abort = &reinterpret_cast<SignalPad*>(c.wsp(c.rank()))->abort;
+  w.timeout_ns = c.config().timeout_ns;
+  w.rank = static_cast<uint32_t>(c.rank());
   const int grid = static_cast<int>(std::min<int64_t>(T, 148 * 4));
   auto* r4 = static_cast<uint4*>(residual);
   const auto* w4 = static_cast<const uint4*>(weight);
   auto* o4 = static_cast<uint4*>(out);
   const int t = static_cast<int>(T), h = static_cast<int>(H), ws = c.world_size();
+  const int m_tiles = h / 128;
   switch (ppt_for(H)) {
-    case 1: k_slots_rmsnorm<1><<<grid, kFThreads, 0, s>>>(base, epoch_word, L.fused_off, L.fused_bytes, ws, splits, r4, w4, o4, t, h, eps); break;
-    case 2: k_slots_rmsnorm<2><<<grid, kFThreads, 0, s>>>(base, epoch_word, L.fused_off, L.fused_bytes, ws, splits, r4, w4, o4, t, h, eps); break;
-    case 4: k_slots_rmsnorm<4><<<grid, kFThreads, 0, s>>>(base, epoch_word, L.fused_off, L.fused_bytes, ws, splits, r4, w4, o4, t, h, eps); break;
-    default: k_slots_rmsnorm<8><<<grid, kFThreads, 0, s>>>(base, epoch_word, L.fused_off, L.fused_bytes, ws, splits, r4, w4, o4, t, h, eps); break;
+    case 1: k_slots_rmsnorm<1><<<grid, kFThreads, 0, s>>>(base, L.fused_off, L.fused_bytes, ws, tile_tokens, m_tiles, w, r4, w4, o4, t, h, eps); break;
+    case 2: k_slots_rmsnorm<2><<<grid, kFThreads, 0, s>>>(base, L.fused_off, L.fused_bytes, ws, tile_tokens, m_tiles, w, r4, w4, o4, t, h, eps); break;
+    case 4: k_slots_rmsnorm<4><<<grid, kFThreads, 0, s>>>(base, L.fused_off, L.fused_bytes, ws, tile_tokens, m_tiles, w, r4, w4, o4, t, h, eps); break;
+    default: k_slots_rmsnorm<8><<<grid, kFThreads, 0, s>>>(base, L.fused_off, L.fused_bytes, ws, tile_tokens, m_tiles, w, r4, w4, o4, t, h, eps); break;
   }
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string("slots rmsnorm launch failed: ") + cudaGetErrorString(e));

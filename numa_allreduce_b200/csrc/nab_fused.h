@@ -33,14 +33,14 @@ int emulate_fused_allreduce_rmsnorm(const std::vector<Communicator*>& comms, cud
                                     const std::vector<void*>& outs, int64_t T, int64_t H, float eps,
                                     int algo);
 
-// Second half of the fused GEMM + allreduce: every rank's [T, H] partial is
-// already in this rank's one-shot slots (written by the GEMM epilogue of the
-// call whose epoch the signal pad holds); adds them in rank order with the
-// residual and applies RMSNorm. No communication.
-// With splits > 1 every slot holds `splits` fp32 partials [split][T][H],
-// added rank by rank, split by split.
+// Second half of the fused GEMM + allreduce: every rank's bf16 [T, H] GEMM
+// output lands in this rank's fused slots (written by the GEMM epilogues of
+// the call whose epoch the signal pad holds), one flag per 128-feature x
+// `tile_tokens`-token tile and rank; waits for the flags of each row's tiles
+// (bounded), adds the ranks' rows in rank order with the residual and
+// applies RMSNorm. tile_tokens == 0 skips the waits (slots already complete).
 void slots_rmsnorm(Communicator& c, cudaStream_t s, void* residual, const void* weight, void* out, int64_t T,
-                   int64_t H, float eps, int splits = 1);
+                   int64_t H, float eps, int tile_tokens);
 
 // Local residual add + RMSNorm (no communication): the world-size-1 path and
 // the norm of the unfused baseline.

@@ -10,22 +10,33 @@
 namespace nab {
 
 // y[T, N] = x[T, K] . wt[N, K]^T in bf16 with fp32 accumulation. N must be a
-// multiple of 128 and K of 64. With splits > 1 the K loop is split over that
-// many CTAs per tile; splitk_ws must then hold splits * T * N floats.
-void gemm_bf16(cudaStream_t s, const void* wt, const void* x, void* y, int T, int N, int K, float* splitk_ws,
-               int64_t splitk_ws_floats, int splits);
+// multiple of 128 and K of 64. With splits > 1 the K loop of each output tile
+// is split over that many CTAs (at most 16), launched as one thread-block
+// cluster that adds the fp32 partials in split order over distributed
+// shared memory; splits <= 0 picks the count (gemm_splits_for).
+// packed: wt is in the tiled layout of pack_weight_tiles — [N/128][K/64] tiles
+// of 128 rows x 64 columns, each 16 KB contiguous — so every weight TMA load
+// reads one contiguous block of HBM instead of 128 rows 2K bytes apart.
+// swiglu: every 128-row tile of wt holds 64 gate rows followed by the 64
+// matching up rows (interleave_gate_up); y is then [T, N/2] with
+// y = silu(gate) * up computed from the fp32 accumulators.
+void gemm_bf16(cudaStream_t s, const void* wt, const void* x, void* y, int T, int N, int K, int splits,
+               bool packed = false, bool swiglu = false);
 
-// Split count that gives enough CTAs to stream the weight from every SM.
+// Split count that balances the CTAs over the SMs.
 int gemm_splits_for(int T, int N, int K, int sms);
+// Clusters of cs CTAs of the bn-token-wide kernel the device runs at once.
+int gemm_active_clusters(int bn, int cs);
 
-// Row-parallel layer tail in two launches: the GEMM whose epilogue stores its
-// bf16 partial tiles into every rank's slot over NVLink (with a per-tile flag
-// exchange), then the rank-order sum + residual add + RMSNorm from the slots.
+// Row-parallel layer tail in two launches: the GEMM whose epilogue stores
+// each finished bf16 output tile into this rank's slot on every rank over
+// NVLink and raises the tile's flag there, then the kernel that waits for
+// each row's tiles and does the rank-order sum + residual add + RMSNorm.
 // residual is updated in place; out receives the normalised activations.
-// splits <= 0 picks the split-K factor; with more than one split the
-// partials travel in fp32 (one per split), otherwise in bf16. Returns the
-// split count used.
+// splits as for gemm_bf16 (split partials are added on this GPU, so only
+// bf16 tiles cross NVLink). Returns the split count used.
 int gemm_allreduce_rmsnorm(Communicator& c, cudaStream_t s, const void* wt, const void* x, void* residual,
-                           const void* weight, void* out, int T, int N, int K, float eps, int splits);
+                           const void* weight, void* out, int T, int N, int K, float eps, int splits,
+                           bool packed = false);
 
 }  // namespace nab

@@ -12,15 +12,22 @@
 //            commits each stage back to the producer;
 //   warps 2-5  epilogue: tcgen05.ld the accumulator, convert to bf16, stage
 //            the tile in shared memory as [token][feature] and write it out.
-// Split-K (grid dimension `splits`) gives small-N layers enough CTAs: each
-// split writes an fp32 partial and a second kernel adds them in split order.
+// Split-K: the `splits` CTAs of one output tile (at most 16) form a thread-
+// block cluster. Each leaves its fp32 accumulator tile in its own shared
+// memory; after a cluster barrier every CTA adds one slice of the tile over
+// all splits in split order (distributed shared memory loads), so the
+// reduction needs no global workspace and no second kernel.
+//
+// Programmatic dependent launch: the producer fills the ring with weight
+// tiles before griddepcontrol.wait, so the weight stream of a decode-step
+// GEMM starts while the kernel before it is still running.
 //
 // Fused with the allreduce (no counterpart in the reference, which has no
-// fused ops): the epilogue stores the bf16 partial tile straight into every
-// rank's one-shot slot over NVLink (its own slot included), then exchanges a
-// per-tile flag with the same CTA on every peer. When the kernel ends every
-// peer's partials of every tile are in local memory, and a second kernel adds
-// them in rank order with the residual and applies RMSNorm.
+// fused ops): each slice is stored straight into this rank's slot on every
+// rank over NVLink (its own included); once the whole tile is stored the
+// tile's flag is raised on every rank. A second kernel waits for the flags of
+// each row's tiles and adds the ranks' rows in rank order with the residual,
+// then applies RMSNorm. The GEMM itself never waits for a peer.
 //
 // Every mbarrier and flag wait is bounded; on expiry the CTA stops issuing,
 // waits (bounded) for its TMA loads in flight, frees its TMEM and returns.
@@ -28,6 +35,9 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <climits>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <stdexcept>
@@ -49,6 +59,7 @@ constexpr int kGemmThreads = 192;
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // 128 bytes of bf16: one swizzle atom row
 constexpr int kABytes = kBM * kBK * 2;
+constexpr int kMaxSplits = 16;  // CTAs per output tile = cluster size (16 needs the non-portable opt-in)
 
 struct GemmArgs {
   int M;          // output features (rows of Wt), multiple of 128
@@ -56,11 +67,13 @@ struct GemmArgs {
   int T;          // tokens
   int m_tiles;
   int n_tiles;
-  int splits;
+  int splits;     // CTAs per output tile = cluster size (1..16)
   int kb_per_split;
   int fused;
-  __nv_bfloat16* out;  // [T, M] bf16 (splits == 1, not fused)
-  float* partial;      // [splits, T, M] fp32 (splits > 1)
+  int a_packed;   // Wt stored as contiguous 128 x 64 tiles (pack_weight layout)
+  int swiglu;     // each 128-row tile is 64 gate rows then the 64 matching up
+                  // rows; out[T, M/2] = silu(gate) * up
+  __nv_bfloat16* out;  // [T, M] bf16 (not fused)
   // fused allreduce epilogue
   char* wsp[kMaxRanks];
   int rank;
@@ -72,17 +85,23 @@ struct GemmArgs {
   uint64_t timeout_ns;
 };
 
+// Small token tiles (decode) are bound by streaming the weight: 2 CTAs per SM
+// with a shorter ring keep more bytes in flight per SM than one CTA with a
+// long ring. Larger tiles use one CTA per SM and a deeper ring. The ring must
+// also hold the fp32 accumulator tile [BN][128] for the split-K exchange.
 template <int BN>
 struct GemmCfg {
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = BN <= 64 ? 8 : (BN == 128 ? 6 : 4);
+  static constexpr int kStages = BN == 16 ? 6 : (BN == 32 ? 5 : (BN == 64 ? 8 : (BN == 128 ? 6 : 4)));
+  static constexpr int kCtasPerSm = BN <= 32 ? 2 : 1;
   static constexpr int kTmemCols = BN < 32 ? 32 : BN;
   static constexpr int kSmem = kStages * kStageBytes + 1024;  // + alignment slack
+  static_assert(kStages * kStageBytes >= BN * kBM * 4, "accumulator tile must fit the ring");
 };
 
 template <int BN>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(kGemmThreads, GemmCfg<BN>::kCtasPerSm)
     k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ GemmArgs g) {
   using Cfg = GemmCfg<BN>;
@@ -94,22 +113,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __shared__ __align__(8) uint64_t accum_bar;
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
+  __shared__ uint32_t s_epoch;
   volatile int* abort_flag = &s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile = blockIdx.x;
+  // the splits of one output tile are consecutive CTAs: one cluster
+  const int split = blockIdx.x % g.splits;
+  const int tile = blockIdx.x / g.splits;
   const int m_tile = tile % g.m_tiles;
-  const int rest = tile / g.m_tiles;
-  const int n_tile = rest % g.n_tiles;
-  const int split = rest / g.n_tiles;
+  const int n_tile = tile / g.m_tiles;
   const int m0 = m_tile * kBM;
   const int t0 = n_tile * BN;
   const int kb0 = split * g.kb_per_split;
   const int kb1 = min(g.K / kBK, kb0 + g.kb_per_split);
-  const int nkb = kb1 - kb0;
+  const int nkb = max(0, kb1 - kb0);
+  const int rows = min(BN, g.T - t0);  // valid tokens of this tile
 
-  uint32_t epoch = 0;
-  if (g.fused) epoch = begin_call(g.wsp, g.rank);
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       sm100::mbar_init(&full_bar[s], 1);
@@ -118,6 +137,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     sm100::mbar_init(&accum_bar, 1);
     sm100::fence_barrier_init();
     s_abort = 0;
+    s_epoch = 0;
     sm100::prefetch_tensormap(&tmA);
     sm100::prefetch_tensormap(&tmB);
   }
@@ -125,6 +145,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     sm100::tmem_alloc(&s_tmem, Cfg::kTmemCols);
     sm100::tmem_relinquish();
   }
+  // a programmatically dependent launch after this one may start scheduling
+  // (it still waits for this grid to complete before it reads our output)
+  if (threadIdx.x == 0) sm100::griddep_launch_dependents();
   sm100::tc_fence_before();
   __syncthreads();
   sm100::tc_fence_after();
@@ -132,8 +155,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   auto fail = [&](uint32_t stage) {
     if (g.err != nullptr && !*abort_flag) {
-      WaitCtx w = make_wait(g.err, g.err_host, g.timeout_ns, g.wsp, g.rank, epoch);
-      if (g.fused) record_failure(w, kErrTimeout, 0xffffffffu, stage, 0);
+      WaitCtx w = make_wait(g.err, g.err_host, g.timeout_ns, g.wsp, g.rank, 0);
+      record_failure(w, kErrTimeout, static_cast<uint32_t>(g.rank), stage, 0);
     }
     *abort_flag = 1;
   };
@@ -141,17 +164,33 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------- TMA producer
     if (lane == 0) {
-      int issued = 0;
-      for (int i = 0; i < nkb; ++i) {
+      // weight tile (m_tile, kb): row-major Wt, or the packed layout in which
+      // each 128 x 64 tile is 16 KB of contiguous memory (one DRAM stream)
+      auto a_x = [&](int kb) { return g.a_packed ? 0 : kb * kBK; };
+      auto a_y = [&](int kb) { return g.a_packed ? (m_tile * (g.K / kBK) + kb) * kBM : m0; };
+      // The weight does not depend on the previous kernel in the stream:
+      // fill the ring with weight tiles first, and only then wait (with a
+      // programmatic dependent launch) for the activations to be ready.
+      const int pre = min(S, nkb);
+      for (int i = 0; i < pre; ++i) {
+        uint8_t* sa = smem + i * Cfg::kStageBytes;
+        sm100::mbar_arrive_expect_tx(&full_bar[i], Cfg::kStageBytes);
+        sm100::tma_load_2d(sa, &tmA, a_x(kb0 + i), a_y(kb0 + i), &full_bar[i]);
+      }
+      sm100::griddep_wait();
+      for (int i = 0; i < pre; ++i)
+        sm100::tma_load_2d(smem + i * Cfg::kStageBytes + kABytes, &tmB, (kb0 + i) * kBK, t0, &full_bar[i]);
+      int issued = pre;
+      for (int i = pre; i < nkb; ++i) {
         const int s = i % S;
-        if (i >= S && !sm100::mbar_wait(&empty_bar[s], ((i / S) - 1) & 1, g.timeout_ns, abort_flag)) {
+        if (!sm100::mbar_wait(&empty_bar[s], ((i / S) - 1) & 1, g.timeout_ns, abort_flag)) {
           fail(kStageGemmAR);
           break;
         }
         if (*abort_flag) break;
         uint8_t* sa = smem + s * Cfg::kStageBytes;
         sm100::mbar_arrive_expect_tx(&full_bar[s], Cfg::kStageBytes);
-        sm100::tma_load_2d(sa, &tmA, (kb0 + i) * kBK, m0, &full_bar[s]);
+        sm100::tma_load_2d(sa, &tmA, a_x(kb0 + i), a_y(kb0 + i), &full_bar[s]);
         sm100::tma_load_2d(sa + kABytes, &tmB, (kb0 + i) * kBK, t0, &full_bar[s]);
         ++issued;
       }
@@ -184,129 +223,118 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       sm100::mma_commit(&accum_bar);  // fires once every MMA above completed
     }
   } else {
-    // ---------------------------------------------------------- epilogue
+    // ------------------------------------- epilogue, part 1: TMEM -> smem
+    // The accumulator goes to this CTA's (now idle) ring as fp32
+    // [token][feature]; a split with no k-blocks contributes zeros.
     const int q = warp & 3;        // TMEM lane quarter this warp may access
     const int row = q * 32 + lane;  // feature within the tile
-    const int et = threadIdx.x - 64;
-    if (!sm100::mbar_wait(&accum_bar, 0, g.timeout_ns, abort_flag)) fail(kStageGemmAR);
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-    const bool ok = !*abort_flag;  // uniform over the epilogue warps
+    if (nkb > 0 && !sm100::mbar_wait(&accum_bar, 0, g.timeout_ns, abort_flag)) fail(kStageGemmAR);
     sm100::tc_fence_after();
-    const int rows = min(BN, g.T - t0);  // valid tokens of this tile
-    if (ok && nkb > 0) {
-      if (g.splits > 1 && !g.fused) {
-        // fp32 partial: [split][t][m]
-        float* dstp = g.partial + (static_cast<int64_t>(split) * g.T) * g.M + m0 + row;
+    float* acc = reinterpret_cast<float*>(smem);
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 16) {
-          uint32_t r[16];
-          sm100::tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, r);
-          sm100::tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 16; ++j)
-            if (c0 + j < rows) dstp[static_cast<int64_t>(t0 + c0 + j) * g.M] = __uint_as_float(r[j]);
-        }
-      } else if (g.splits > 1) {
-        // fused split-K: stage [token][feature] fp32 and store it into every
-        // rank's slot as [split][t][m] fp32
-        float* st = reinterpret_cast<float*>(smem);
-#pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 16) {
-          uint32_t r[16];
-          sm100::tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, r);
-          sm100::tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 16; ++j) st[(c0 + j) * kBM + row] = __uint_as_float(r[j]);
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        const uint4* st4 = reinterpret_cast<const uint4*>(st);
-        const int nvec = rows * (kBM / 4);  // 32 x 16 B per token row
-        const int parity = epoch & 1;
-        for (int idx = et; idx < nvec; idx += 128) {
-          const int t = idx >> 5, v = idx & 31;
-          const uint4 val = st4[idx];
-          const int64_t off = ((static_cast<int64_t>(split) * g.T + t0 + t) * g.M + m0) * 4;
-          for (int k = 0; k < g.ws; ++k) {
-            const int dst = (g.rank + k) % g.ws;
-            char* slot = g.wsp[dst] + g.slot_off + (static_cast<int64_t>(parity) * g.ws + g.rank) * g.slot_bytes;
-            reinterpret_cast<uint4*>(slot + off)[v] = val;
-          }
-        }
+    for (int c0 = 0; c0 < BN; c0 += 16) {
+      if (c0 >= rows) break;
+      uint32_t r[16];
+      if (nkb > 0) {
+        sm100::tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, r);
+        sm100::tmem_wait_ld();
       } else {
-        // stage [token][feature] bf16 in the (now idle) pipeline memory
-        __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(smem);
-#pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 16) {
-          uint32_t r[16];
-          sm100::tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, r);
-          sm100::tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 16; ++j) st[(c0 + j) * kBM + row] = __float2bfloat16_rn(__uint_as_float(r[j]));
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        const uint4* st4 = reinterpret_cast<const uint4*>(st);
-        const int nvec = rows * (kBM / 8);  // 16 x 16 B per token row
-        if (!g.fused) {
-          for (int idx = et; idx < nvec; idx += 128) {
-            const int t = idx >> 4, v = idx & 15;
-            reinterpret_cast<uint4*>(g.out + static_cast<int64_t>(t0 + t) * g.M + m0)[v] = st4[idx];
-          }
-        } else {
-          const int parity = epoch & 1;
-          for (int idx = et; idx < nvec; idx += 128) {
-            const int t = idx >> 4, v = idx & 15;
-            const uint4 val = st4[idx];
-            const int64_t off = (static_cast<int64_t>(t0 + t) * g.M + m0) * 2;
-            for (int k = 0; k < g.ws; ++k) {
-              const int dst = (g.rank + k) % g.ws;  // stagger the peers
-              char* slot = g.wsp[dst] + g.slot_off + (static_cast<int64_t>(parity) * g.ws + g.rank) * g.slot_bytes;
-              reinterpret_cast<uint4*>(slot + off)[v] = val;
-            }
-          }
-        }
+        for (int j = 0; j < 16; ++j) r[j] = 0u;
       }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) acc[(c0 + j) * kBM + row] = __uint_as_float(r[j]);
     }
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-    if (g.fused && !*abort_flag) {
-      // exchange this tile's flag with the same CTA on every peer
-      if (et < g.ws - 1) {
-        const int peer = (g.rank + 1 + et) % g.ws;
-        const uint64_t seq = make_seq(epoch, 0);
-        st_release_sys(&pad_at(g.wsp, peer)->flags[kFlagGemm].v[tile][g.rank], seq);
-        WaitCtx w = make_wait(g.err, g.err_host, g.timeout_ns, g.wsp, g.rank, epoch);
-        if (!wait_geq(&pad_at(g.wsp, g.rank)->flags[kFlagGemm].v[tile][peer], seq, w, peer, kStageGemmAR))
-          *abort_flag = 1;
+    if (g.fused && threadIdx.x == 64) {
+      // The epoch of the previous call is final once the kernels before
+      // this launch have completed.
+      sm100::griddep_wait();
+      s_epoch = ld_volatile_u32(&pad_at(g.wsp, g.rank)->epoch) + 1u;
+    }
+  }
+  // All splits' accumulators are in their CTAs' shared memory.
+  sm100::tc_fence_before();
+  if (g.splits > 1) sm100::cluster_sync(); else __syncthreads();
+
+  // ------------------------------ epilogue, part 2: split reduce + store
+  // The tile's output is [rows][128] features (64 with SwiGLU) = chunks of
+  // 8; the cluster's CTAs take contiguous ranges of chunks, add the splits'
+  // fp32 values in split order (every CTA of the cluster holds one split)
+  // and write bf16.
+  const bool ok = !*abort_flag;
+  if (warp >= 2 && ok) {
+    const int et = threadIdx.x - 64;
+    const int out_cols = g.swiglu ? kBM / 2 : kBM;
+    const int ldo = g.swiglu ? g.M / 2 : g.M;  // output row stride
+    const int cpr = out_cols / 8;               // chunks per token row
+    const int nchunk = rows * cpr;
+    const int per = (nchunk + g.splits - 1) / g.splits;
+    const int c_beg = split * per, c_end = min(nchunk, c_beg + per);
+    const uint32_t acc_addr = sm100::smem_u32(smem);
+    const int parity = s_epoch & 1;
+    // 8 consecutive fp32 accumulator values at byte offset `off`, summed over
+    // the splits in split order
+    auto gather8 = [&](uint32_t off, float (&v)[8]) {
+      if (g.splits == 1) {
+        const float4 lo = *reinterpret_cast<const float4*>(smem + off);
+        const float4 hi = *reinterpret_cast<const float4*>(smem + off + 16);
+        v[0] = lo.x; v[1] = lo.y; v[2] = lo.z; v[3] = lo.w;
+        v[4] = hi.x; v[5] = hi.y; v[6] = hi.z; v[7] = hi.w;
+        return;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = 0.f;
+      for (int sp = 0; sp < g.splits; ++sp) {
+        const uint32_t ra = sm100::dsmem_addr(acc_addr + off, static_cast<uint32_t>(sp));
+        const float4 lo = sm100::ld_dsmem_f4(ra), hi = sm100::ld_dsmem_f4(ra + 16);
+        v[0] += lo.x; v[1] += lo.y; v[2] += lo.z; v[3] += lo.w;
+        v[4] += hi.x; v[5] += hi.y; v[6] += hi.z; v[7] += hi.w;
+      }
+    };
+    for (int c = c_beg + et; c < c_end; c += 128) {
+      const int t = c / cpr, f = (c % cpr) * 8;
+      float v[8];
+      gather8(static_cast<uint32_t>((t * kBM + f) * 4), v);
+      if (g.swiglu) {
+        float u[8];
+        gather8(static_cast<uint32_t>((t * kBM + kBM / 2 + f) * 4), u);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = v[j] / (1.f + __expf(-v[j])) * u[j];
+      }
+      uint4 packed;
+      __nv_bfloat162 h[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+      packed.x = *reinterpret_cast<uint32_t*>(&h[0]);
+      packed.y = *reinterpret_cast<uint32_t*>(&h[1]);
+      packed.z = *reinterpret_cast<uint32_t*>(&h[2]);
+      packed.w = *reinterpret_cast<uint32_t*>(&h[3]);
+      const int64_t eoff = static_cast<int64_t>(t0 + t) * ldo + m_tile * out_cols + f;  // element offset
+      if (!g.fused) {
+        *reinterpret_cast<uint4*>(g.out + eoff) = packed;
+      } else {
+        // into this rank's slot on every rank (its own included), staggered
+        for (int k = 0; k < g.ws; ++k) {
+          const int dst = (g.rank + k) % g.ws;
+          char* slot = g.wsp[dst] + g.slot_off + (static_cast<int64_t>(parity) * g.ws + g.rank) * g.slot_bytes;
+          *reinterpret_cast<uint4*>(slot + eoff * 2) = packed;
+        }
       }
     }
   }
-  sm100::tc_fence_before();
-  __syncthreads();
+  // No CTA leaves while a peer of its cluster may still read its shared
+  // memory; with the allreduce, every slice of the tile is stored.
+  if (g.splits > 1) sm100::cluster_sync(); else __syncthreads();
+  if (g.fused && split == 0 && threadIdx.x < g.ws && !*abort_flag) {
+    // the tile is in every rank: raise its flag there (the norm kernel waits)
+    const int dst = (g.rank + threadIdx.x) % g.ws;
+    st_release_sys(&pad_at(g.wsp, dst)->gemm_flags[n_tile * g.m_tiles + m_tile][g.rank], make_seq(s_epoch, 0));
+  }
   if (warp == 1) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tmem, Cfg::kTmemCols);
   }
-  if (g.fused) end_call(g.wsp, g.rank, epoch);
-}
-
-// Adds the split-K partials in split order and rounds to bf16.
-__global__ void k_splitk_reduce(const float* __restrict__ partial, __nv_bfloat16* __restrict__ out, int splits,
-                                int64_t n4) {
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += stride) {
-    float4 a = reinterpret_cast<const float4*>(partial)[i];
-    for (int s = 1; s < splits; ++s) {
-      const float4 b = reinterpret_cast<const float4*>(partial + s * n4 * 4)[i];
-      a.x += b.x;
-      a.y += b.y;
-      a.z += b.z;
-      a.w += b.w;
-    }
-    __nv_bfloat162 lo = __floats2bfloat162_rn(a.x, a.y), hi = __floats2bfloat162_rn(a.z, a.w);
-    uint2 v;
-    v.x = *reinterpret_cast<uint32_t*>(&lo);
-    v.y = *reinterpret_cast<uint32_t*>(&hi);
-    reinterpret_cast<uint2*>(out)[i] = v;
-  }
+  if (g.fused) end_call(g.wsp, g.rank, s_epoch);
 }
 
 // ------------------------------------------------------------ tensor maps --
@@ -348,32 +376,128 @@ int pick_bn(int T) {
   return 256;
 }
 
+// Launch with the split CTAs of a tile as one thread-block cluster and, when
+// `pdl`, as a programmatic dependent launch (the weight prefetch overlaps the
+// tail of the previous kernel in the stream).
 template <int BN>
-void launch_bn(const CUtensorMap& a, const CUtensorMap& b, const GemmArgs& g, int grid, cudaStream_t s) {
+void launch_bn(const CUtensorMap& a, const CUtensorMap& b, const GemmArgs& g, int grid, cudaStream_t s, bool pdl) {
   using Cfg = GemmCfg<BN>;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev & 63]) {
     NAB_CUDA_CHECK(cudaFuncSetAttribute(k_gemm_bf16<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem));
+    NAB_CUDA_CHECK(cudaFuncSetAttribute(k_gemm_bf16<BN>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     attr_set[dev & 63] = true;
   }
-  k_gemm_bf16<BN><<<grid, kGemmThreads, Cfg::kSmem, s>>>(a, b, g);
-  const cudaError_t e = cudaGetLastError();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = Cfg::kSmem;
+  cfg.stream = s;
+  cudaLaunchAttribute attrs[2];
+  int n = 0;
+  attrs[n].id = cudaLaunchAttributeClusterDimension;
+  attrs[n].val.clusterDim.x = g.splits;
+  attrs[n].val.clusterDim.y = 1;
+  attrs[n].val.clusterDim.z = 1;
+  ++n;
+  if (pdl) {
+    attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = n;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_bf16<BN>, a, b, g);
   if (e != cudaSuccess) throw std::runtime_error(std::string("GEMM launch failed: ") + cudaGetErrorString(e));
 }
 
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("NAB_GEMM_PDL");
+    return v == nullptr || std::strcmp(v, "0") != 0;
+  }();
+  return on;
+}
+
 void launch(const void* wt, const void* x, const GemmArgs& g, int bn, cudaStream_t s) {
-  const CUtensorMap a = make_map(wt, g.M, g.K, kBM);
+  const CUtensorMap a = g.a_packed ? make_map(wt, static_cast<int64_t>(g.M) * (g.K / kBK), kBK, kBM)
+                                   : make_map(wt, g.M, g.K, kBM);
   const CUtensorMap b = make_map(x, g.T, g.K, bn);
   const int grid = g.m_tiles * g.n_tiles * g.splits;
+  const bool pdl = pdl_enabled();
   switch (bn) {
-    case 16: launch_bn<16>(a, b, g, grid, s); break;
-    case 32: launch_bn<32>(a, b, g, grid, s); break;
-    case 64: launch_bn<64>(a, b, g, grid, s); break;
-    case 128: launch_bn<128>(a, b, g, grid, s); break;
-    default: launch_bn<256>(a, b, g, grid, s); break;
+    case 16: launch_bn<16>(a, b, g, grid, s, pdl); break;
+    case 32: launch_bn<32>(a, b, g, grid, s, pdl); break;
+    case 64: launch_bn<64>(a, b, g, grid, s, pdl); break;
+    case 128: launch_bn<128>(a, b, g, grid, s, pdl); break;
+    default: launch_bn<256>(a, b, g, grid, s, pdl); break;
   }
+}
+
+int sm_count() {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
+// Clusters of `cs` CTAs of the BN-wide kernel that fit on the device at once
+// (cudaOccupancyMaxActiveClusters: accounts for shared memory, CTAs per SM
+// and the placement of a cluster inside one GPC). 0 if it cannot launch.
+template <int BN>
+int active_clusters_bn(int cs) {
+  using Cfg = GemmCfg<BN>;
+  NAB_CUDA_CHECK(cudaFuncSetAttribute(k_gemm_bf16<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem));
+  NAB_CUDA_CHECK(cudaFuncSetAttribute(k_gemm_bf16<BN>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(cs * 64);
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = Cfg::kSmem;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = cs;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, k_gemm_bf16<BN>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+int active_clusters(int bn, int cs) {
+  static std::mutex mu;
+  static std::unordered_map<int, int> cache;  // (device, bn, cs) -> clusters
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int key = (dev << 16) | (bn << 5) | cs;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  int n = 0;
+  switch (bn) {
+    case 16: n = active_clusters_bn<16>(cs); break;
+    case 32: n = active_clusters_bn<32>(cs); break;
+    case 64: n = active_clusters_bn<64>(cs); break;
+    case 128: n = active_clusters_bn<128>(cs); break;
+    default: n = active_clusters_bn<256>(cs); break;
+  }
+  cache[key] = n;
+  return n;
+}
+
+// Split count actually launched: every split gets at least one k-block.
+void set_splits(GemmArgs& g, int splits, int bn) {
+  const int kb = g.K / kBK;
+  splits = std::max(1, std::min({splits, kMaxSplits, kb}));
+  while (splits > 1 && active_clusters(bn, splits) == 0) --splits;
+  g.kb_per_split = (kb + splits - 1) / splits;
+  g.splits = (kb + g.kb_per_split - 1) / g.kb_per_split;
 }
 
 void check_shape(int T, int N, int K) {
@@ -383,52 +507,59 @@ void check_shape(int T, int N, int K) {
 
 }  // namespace
 
+int gemm_active_clusters(int bn, int cs) { return active_clusters(bn, cs); }
+
 int gemm_splits_for(int T, int N, int K, int sms) {
+  (void)sms;  // the device's own occupancy answer accounts for the SMs
   const int bn = pick_bn(T);
   const int tiles = (N / kBM) * ((T + bn - 1) / bn);
   const int kb = K / kBK;
-  int splits = 1;
-  // enough CTAs to stream the weight from every SM, at least 8 k-blocks each
-  while (tiles * splits * 2 <= sms && kb / (splits * 2) >= 8) splits *= 2;
-  return splits;
+  // Time model in k-blocks: waves of co-resident clusters x (k-blocks per
+  // split + a fixed cost per CTA for its prologue and epilogue). Ties go to
+  // fewer splits.
+  const int fixed = bn <= 32 ? 3 : 2;
+  int best = 1;
+  int64_t best_cost = INT64_MAX;
+  for (int sp = 1; sp <= kMaxSplits && sp <= kb; ++sp) {
+    const int per = (kb + sp - 1) / sp;
+    if ((kb + per - 1) / per != sp) continue;  // would leave a split without work
+    const int clusters = active_clusters(bn, sp);
+    if (clusters == 0) continue;
+    const int64_t waves = (tiles + clusters - 1) / clusters;
+    const int64_t cost = waves * (per + fixed);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = sp;
+    }
+  }
+  return best;
 }
 
-void gemm_bf16(cudaStream_t s, const void* wt, const void* x, void* y, int T, int N, int K, float* splitk_ws,
-               int64_t splitk_ws_floats, int splits) {
+void gemm_bf16(cudaStream_t s, const void* wt, const void* x, void* y, int T, int N, int K, int splits,
+               bool packed, bool swiglu) {
   check_shape(T, N, K);
   GemmArgs g{};
+  g.a_packed = packed ? 1 : 0;
+  g.swiglu = swiglu ? 1 : 0;
   const int bn = pick_bn(T);
   g.M = N;
   g.K = K;
   g.T = T;
   g.m_tiles = N / kBM;
   g.n_tiles = (T + bn - 1) / bn;
-  g.splits = std::max(1, splits);
-  g.kb_per_split = (K / kBK + g.splits - 1) / g.splits;
-  g.splits = (K / kBK + g.kb_per_split - 1) / g.kb_per_split;
+  set_splits(g, splits > 0 ? splits : gemm_splits_for(T, N, K, sm_count()), bn);
   g.out = static_cast<__nv_bfloat16*>(y);
   g.timeout_ns = 2000000000ull;
-  if (g.splits > 1) {
-    const int64_t need = static_cast<int64_t>(g.splits) * T * N;
-    if (splitk_ws == nullptr || splitk_ws_floats < need)
-      throw std::invalid_argument("split-K GEMM needs a workspace of splits * T * N floats");
-    g.partial = splitk_ws;
-  }
   launch(wt, x, g, bn, s);
-  if (g.splits > 1) {
-    const int64_t n4 = static_cast<int64_t>(T) * N / 4;
-    const int blocks = static_cast<int>(std::min<int64_t>((n4 + 255) / 256, 148 * 4));
-    k_splitk_reduce<<<blocks, 256, 0, s>>>(splitk_ws, static_cast<__nv_bfloat16*>(y), g.splits, n4);
-    const cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) throw std::runtime_error(std::string("split-K reduce failed: ") + cudaGetErrorString(e));
-  }
 }
 
 int gemm_allreduce_rmsnorm(Communicator& c, cudaStream_t s, const void* wt, const void* x, void* residual,
-                           const void* weight, void* out, int T, int N, int K, float eps, int splits) {
+                           const void* weight, void* out, int T, int N, int K, float eps, int splits, bool packed) {
   check_shape(T, N, K);
   const Layout& L = c.layout();
   if (c.world_size() == 1) throw std::invalid_argument("GEMM+allreduce needs a world size of at least 2");
+  if (static_cast<int64_t>(T) * N * 2 > L.fused_bytes)
+    throw std::invalid_argument("GEMM+allreduce: the output exceeds the fused slot");
   const int bn = pick_bn(T);
   GemmArgs g{};
   g.M = N;
@@ -436,23 +567,10 @@ int gemm_allreduce_rmsnorm(Communicator& c, cudaStream_t s, const void* wt, cons
   g.T = T;
   g.m_tiles = N / kBM;
   g.n_tiles = (T + bn - 1) / bn;
-  if (splits <= 0) {
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    splits = gemm_splits_for(T, N, K, sms);
-  }
-  // one split: bf16 partials; several: fp32 partials, one per split. Fewer
-  // splits until the partials fit the slot.
-  auto need = [&](int sp) {
-    return sp > 1 ? static_cast<int64_t>(sp) * T * N * 4 : static_cast<int64_t>(T) * N * 2;
-  };
-  while (splits > 1 && need(splits) > L.fused_bytes) splits /= 2;
-  g.kb_per_split = (K / kBK + splits - 1) / splits;
-  g.splits = (K / kBK + g.kb_per_split - 1) / g.kb_per_split;
-  if (need(g.splits) > L.fused_bytes) throw std::invalid_argument("GEMM+allreduce: partials exceed the fused slot");
+  if (g.m_tiles * g.n_tiles > kGemmMaxTiles) throw std::invalid_argument("GEMM+allreduce: too many output tiles");
+  set_splits(g, splits > 0 ? splits : gemm_splits_for(T, N, K, sm_count()), bn);
   g.fused = 1;
-  if (g.m_tiles * g.n_tiles * g.splits > kMaxBlocks) throw std::invalid_argument("GEMM+allreduce: too many tiles");
+  g.a_packed = packed ? 1 : 0;
   for (int r = 0; r < c.world_size(); ++r) g.wsp[r] = c.wsp(r);
   g.rank = c.rank();
   g.ws = c.world_size();
@@ -463,7 +581,7 @@ int gemm_allreduce_rmsnorm(Communicator& c, cudaStream_t s, const void* wt, cons
   g.timeout_ns = c.config().timeout_ns;
   launch(wt, x, g, bn, s);
   c.count_launch();
-  slots_rmsnorm(c, s, residual, weight, out, T, N, eps, g.splits);
+  slots_rmsnorm(c, s, residual, weight, out, T, N, eps, bn);
   return g.splits;
 }
 

@@ -129,5 +129,38 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
          | (static_cast<uint32_t>(m >> 4) << 24);   // M / 16
 }
 
+// ------------------------------------------------------------- clusters --
+// Barrier over every thread of every CTA in the cluster; the release/acquire
+// pair makes shared-memory writes before it visible cluster-wide after it.
+NAB_DINLINE void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release;\nbarrier.cluster.wait.acquire;" ::: "memory");
+}
+NAB_DINLINE uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+NAB_DINLINE uint32_t dsmem_addr(uint32_t local_smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_smem_addr), "r"(rank));
+  return r;
+}
+NAB_DINLINE float4 ld_dsmem_f4(uint32_t cluster_addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(cluster_addr)
+               : "memory");
+  return v;
+}
+
+// ----------------------------------------------- programmatic dependent launch --
+// Waits until the grids this launch depends on have completed and their
+// memory is visible (returns at once without a programmatic dependency).
+NAB_DINLINE void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets a programmatically dependent launch begin scheduling its CTAs.
+NAB_DINLINE void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 }  // namespace sm100
 }  // namespace nab

@@ -292,23 +292,28 @@ void check_gemm_operand(const at::Tensor& t, const char* name) {
 }
 
 // y[T, N] = x[T, K] . wt[N, K]^T on the tcgen05 tensor cores.
-void gemm(const at::Tensor& x, const at::Tensor& wt, at::Tensor& y, const std::optional<at::Tensor>& ws,
-          int64_t splits) {
+// wt: [N, K] row-major, or (packed) the tiled layout [N * K / 64, 64]; N is
+// y's width (twice that with the SwiGLU epilogue).
+void gemm(const at::Tensor& x, const at::Tensor& wt, at::Tensor& y, int64_t splits, bool packed, bool swiglu) {
   check_gemm_operand(x, "x");
   check_gemm_operand(wt, "wt");
   check_gemm_operand(y, "y");
-  TORCH_CHECK(x.size(1) == wt.size(1) && y.size(0) == x.size(0) && y.size(1) == wt.size(0), "GEMM shape mismatch");
+  const int64_t N = y.size(1) * (swiglu ? 2 : 1), K = x.size(1);
+  TORCH_CHECK(y.size(0) == x.size(0), "GEMM shape mismatch");
+  if (packed) {
+    TORCH_CHECK(wt.size(1) == 64 && wt.size(0) * 64 == N * K, "packed weight must be [N * K / 64, 64]");
+  } else {
+    TORCH_CHECK(wt.size(1) == K && wt.size(0) == N, "GEMM shape mismatch");
+  }
   const at::cuda::OptionalCUDAGuard guard(x.device());
   auto stream = at::cuda::getCurrentCUDAStream().stream();
-  float* wsp = nullptr;
-  int64_t wsn = 0;
-  if (ws.has_value()) {
-    TORCH_CHECK(ws->is_cuda() && ws->scalar_type() == at::kFloat && ws->is_contiguous(), "split-K workspace must be fp32");
-    wsp = ws->data_ptr<float>();
-    wsn = ws->numel();
-  }
-  nab::gemm_bf16(stream, wt.data_ptr(), x.data_ptr(), y.data_ptr(), static_cast<int>(x.size(0)),
-                 static_cast<int>(wt.size(0)), static_cast<int>(x.size(1)), wsp, wsn, static_cast<int>(splits));
+  nab::gemm_bf16(stream, wt.data_ptr(), x.data_ptr(), y.data_ptr(), static_cast<int>(x.size(0)), static_cast<int>(N),
+                 static_cast<int>(K), static_cast<int>(splits), packed, swiglu);
+}
+
+
+int64_t gemm_active_clusters(int64_t bn, int64_t cs) {
+  return nab::gemm_active_clusters(static_cast<int>(bn), static_cast<int>(cs));
 }
 
 int64_t gemm_splits(int64_t T, int64_t N, int64_t K) {
@@ -318,21 +323,25 @@ int64_t gemm_splits(int64_t T, int64_t N, int64_t K) {
 }
 
 void gemm_ar_rmsnorm(fptr_t fa, const at::Tensor& x, const at::Tensor& wt, at::Tensor& residual,
-                     const at::Tensor& weight, at::Tensor& out, double eps, int64_t splits) {
+                     const at::Tensor& weight, at::Tensor& out, double eps, int64_t splits, bool packed) {
   check_gemm_operand(x, "x");
   check_gemm_operand(wt, "wt");
   check_gemm_operand(residual, "residual");
   check_gemm_operand(out, "out");
-  TORCH_CHECK(x.size(1) == wt.size(1) && residual.size(0) == x.size(0) && residual.size(1) == wt.size(0) &&
-                  out.sizes() == residual.sizes(),
-              "GEMM+allreduce shape mismatch");
-  TORCH_CHECK(weight.is_contiguous() && weight.numel() == wt.size(0) && weight.scalar_type() == at::kBFloat16,
+  const int64_t N = residual.size(1), K = x.size(1);
+  TORCH_CHECK(residual.size(0) == x.size(0) && out.sizes() == residual.sizes(), "GEMM+allreduce shape mismatch");
+  if (packed) {
+    TORCH_CHECK(wt.size(1) == 64 && wt.size(0) * 64 == N * K, "packed weight must be [N * K / 64, 64]");
+  } else {
+    TORCH_CHECK(wt.size(1) == K && wt.size(0) == N, "GEMM+allreduce shape mismatch");
+  }
+  TORCH_CHECK(weight.is_contiguous() && weight.numel() == N && weight.scalar_type() == at::kBFloat16,
               "norm weight must be [N] bfloat16");
   const at::cuda::OptionalCUDAGuard guard(x.device());
   auto stream = at::cuda::getCurrentCUDAStream().stream();
   nab::gemm_allreduce_rmsnorm(*C(fa), stream, wt.data_ptr(), x.data_ptr(), residual.data_ptr(), weight.data_ptr(),
-                              out.data_ptr(), static_cast<int>(x.size(0)), static_cast<int>(wt.size(0)),
-                              static_cast<int>(x.size(1)), static_cast<float>(eps), static_cast<int>(splits));
+                              out.data_ptr(), static_cast<int>(x.size(0)), static_cast<int>(N), static_cast<int>(K),
+                              static_cast<float>(eps), static_cast<int>(splits), packed);
 }
 
 void rope_append_op(const at::Tensor& qkv, const at::Tensor& cos_t, const at::Tensor& sin_t, const at::Tensor& pos,
@@ -349,18 +358,25 @@ void rope_append_op(const at::Tensor& qkv, const at::Tensor& cos_t, const at::Te
 }
 
 void decode_attention_op(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
-                         const at::Tensor& pos, at::Tensor& part_ml, at::Tensor& part_o, at::Tensor& out,
-                         int64_t splits) {
+                         const at::Tensor& pos, at::Tensor& part_ml, at::Tensor& part_o, at::Tensor& counters,
+                         at::Tensor& out, int64_t splits) {
   TORCH_CHECK(q.dim() == 3 && q.size(2) == 128 && k_cache.dim() == 4, "decode_attention: shapes");
-  const int64_t B = q.size(0), Hq = q.size(1);
+  const int64_t B = q.size(0), Hq = q.size(1), Hkv = k_cache.size(1);
   TORCH_CHECK(part_ml.numel() >= B * Hq * splits * 2 && part_o.numel() >= B * Hq * splits * 128,
               "decode_attention: scratch too small");
+  TORCH_CHECK(counters.scalar_type() == at::kInt && counters.numel() >= B * Hkv, "decode_attention: counters");
   const at::cuda::OptionalCUDAGuard guard(q.device());
   nab::decode_attention(at::cuda::getCurrentCUDAStream().stream(), q.data_ptr(), k_cache.data_ptr(),
                         v_cache.data_ptr(), pos.data_ptr<int>(), part_ml.data_ptr<float>(), part_o.data_ptr<float>(),
-                        out.data_ptr(), static_cast<int>(B), static_cast<int>(Hq),
-                        static_cast<int>(k_cache.size(1)), static_cast<int>(k_cache.size(2)),
-                        static_cast<int>(splits));
+                        counters.data_ptr<int>(), out.data_ptr(), static_cast<int>(B), static_cast<int>(Hq),
+                        static_cast<int>(Hkv), static_cast<int>(k_cache.size(2)), static_cast<int>(splits));
+}
+
+int64_t attention_splits(int64_t B, int64_t Hkv, int64_t context) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return nab::attention_splits(static_cast<int>(B), static_cast<int>(Hkv), static_cast<int>(context), sms);
 }
 
 void silu_mul_op(const at::Tensor& gu, at::Tensor& out) {
@@ -421,17 +437,19 @@ TORCH_LIBRARY(nab, m) {
   m.def("emulate_fused_ar_rmsnorm(int[] fas, Tensor[] ins, Tensor(a!)[] residuals, Tensor[] weights, "
         "Tensor(b!)[] outs, float eps, int algo) -> ()");
   m.impl("emulate_fused_ar_rmsnorm", c10::kCUDA, &emulate_fused_ar_rmsnorm);
-  m.def("gemm(Tensor x, Tensor wt, Tensor(a!) y, Tensor? ws, int splits) -> ()");
+  m.def("gemm(Tensor x, Tensor wt, Tensor(a!) y, int splits=0, bool packed=False, bool swiglu=False) -> ()");
   m.impl("gemm", c10::kCUDA, &gemm);
   m.def("gemm_splits(int T, int N, int K) -> int", &gemm_splits);
+  m.def("gemm_active_clusters(int bn, int cs) -> int", &gemm_active_clusters);
   m.def("gemm_ar_rmsnorm(int fa, Tensor x, Tensor wt, Tensor(a!) residual, Tensor weight, Tensor(b!) out, "
-        "float eps, int splits=0) -> ()");
+        "float eps, int splits=0, bool packed=False) -> ()");
   m.impl("gemm_ar_rmsnorm", c10::kCUDA, &gemm_ar_rmsnorm);
   m.def("rope_append(Tensor qkv, Tensor cos, Tensor sin, Tensor pos, Tensor(a!) q_out, Tensor(b!) k_cache, "
         "Tensor(c!) v_cache, int Hq, int Hkv) -> ()");
   m.impl("rope_append", c10::kCUDA, &rope_append_op);
   m.def("decode_attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor pos, Tensor(a!) part_ml, "
-        "Tensor(b!) part_o, Tensor(c!) out, int splits) -> ()");
+        "Tensor(b!) part_o, Tensor(d!) counters, Tensor(c!) out, int splits) -> ()");
+  m.def("attention_splits(int B, int Hkv, int context) -> int", &attention_splits);
   m.impl("decode_attention", c10::kCUDA, &decode_attention_op);
   m.def("silu_mul(Tensor gu, Tensor(a!) out) -> ()");
   m.impl("silu_mul", c10::kCUDA, &silu_mul_op);

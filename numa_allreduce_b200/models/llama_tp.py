@@ -6,11 +6,14 @@ projections are column-parallel, o_proj and down_proj row-parallel, so each
 layer ends in two allreduces. Both are fused with the residual add and the
 next RMSNorm:
 
-* ``impl="fused"`` (this library): tcgen05 GEMMs; each row-parallel GEMM
-  stores its partial tiles into every rank's buffer over NVLink and a second
-  kernel adds them with the residual and applies the next RMSNorm (or, for
-  token counts where that is faster, the GEMM plus the fused allreduce +
-  residual + RMSNorm kernel);
+* ``impl="fused"`` (this library): tcgen05 GEMMs on weights in the tiled
+  layout (one contiguous 16 KB block per weight tile), launched as
+  programmatic dependent launches so each weight stream starts during the
+  kernel before; the gate|up GEMM applies SwiGLU in its epilogue; each
+  row-parallel GEMM stores its output tiles into every rank's buffer over
+  NVLink and a second kernel adds them with the residual and applies the
+  next RMSNorm (above the fused slot size: the GEMM plus the fused
+  allreduce + residual + RMSNorm kernel);
 * ``impl="baseline"``: cuBLAS (``F.linear``) + NCCL ``all_reduce`` + residual
   add + ``F.rms_norm``, the unfused stack.
 
@@ -32,7 +35,7 @@ import torch.nn.functional as F
 
 from ..ops import _ext
 from ..ops.fused import fused_allreduce_rmsnorm, rmsnorm_residual
-from ..ops.gemm import gemm, gemm_allreduce_rmsnorm
+from ..ops.gemm import gemm, gemm_allreduce_rmsnorm, gemm_swiglu, interleave_gate_up, pack_weight
 
 
 @dataclass
@@ -75,23 +78,29 @@ class LlamaTPDecoder:
         context: tokens already in the (synthetic) KV cache; the step decodes
             position ``context``.
         impl: ``"fused"`` or ``"baseline"`` (see module docstring).
+        shard_of: with a single GPU, build the shard of a ``shard_of``-way
+            tensor-parallel model (same per-GPU shapes, no allreduce), to
+            study one rank's kernels alone.
     """
 
     def __init__(self, cfg: LlamaConfig, comm, batch: int, context: int, impl: str = "fused", seed: int = 0,
-                 device: torch.device | str = "cuda", attn_splits: int | None = None):
+                 device: torch.device | str = "cuda", attn_splits: int | None = None, shard_of: int | None = None):
         if impl not in ("fused", "baseline"):
             raise ValueError("impl must be 'fused' or 'baseline'")
         self.cfg, self.comm, self.impl = cfg, comm, impl
         self.device = torch.device(device)
         self.world = comm.world_size if comm is not None and not comm.disabled else 1
         self.rank = comm.rank if self.world > 1 else 0
-        if cfg.heads % self.world or cfg.intermediate % self.world:
+        if shard_of is not None and self.world > 1 and shard_of != self.world:
+            raise ValueError("shard_of is for a single GPU (or must equal the world size)")
+        W = shard_of or self.world
+        if cfg.heads % W or cfg.intermediate % W:
             raise ValueError("heads and intermediate size must divide by the world size")
         self.ops = _ext.load()
-        W = self.world
         D = cfg.head_dim
         self.Hq = cfg.heads // W
         self.Hkv = max(1, cfg.kv_heads // W)  # kv heads replicated when W > kv_heads
+        self.tp = W
         self.I = cfg.intermediate // W
         self.B, self.ctx = batch, context
         self.Lmax = _round_up(context + 1, 64)
@@ -118,6 +127,10 @@ class LlamaTPDecoder:
         self.final_norm = torch.ones(H, device=self.device, dtype=torch.bfloat16)
         self.v_local = _round_up((cfg.vocab + W - 1) // W, 128)
         self.lm_head = w(self.v_local, H)
+        # this library's GEMM reads weights in the tiled layout (one
+        # contiguous 16 KB block of HBM per weight tile); built on first use
+        # of the fused path
+        self._packed: dict[tuple[int, str], object] = {}
         # rotary tables
         inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, D, 2, device=self.device, dtype=torch.float64) / D))
         ang = torch.arange(self.Lmax, device=self.device, dtype=torch.float64)[:, None] * inv[None, :]
@@ -135,7 +148,8 @@ class LlamaTPDecoder:
         self.act = torch.empty(batch, self.I, **bf)
         self.y = torch.empty(batch, H, **bf)
         self.logits = torch.empty(batch, self.v_local, **bf)
-        self.splits = attn_splits or max(1, min(32, (context + 1) // 64))
+        self.splits = attn_splits or int(self.ops.attention_splits(batch, self.Hkv, context + 1))
+        self.attn_counters = torch.zeros(batch * self.Hkv, device=self.device, dtype=torch.int32)
         self.part_ml = torch.empty(batch * self.Hq * self.splits * 2, device=self.device, dtype=torch.float32)
         self.part_o = torch.empty(batch * self.Hq * self.splits * D, device=self.device, dtype=torch.float32)
         self.gemm_splits = {}
@@ -143,6 +157,17 @@ class LlamaTPDecoder:
         self._gathered = torch.empty(W * batch * 2, device=self.device, dtype=torch.float32)
 
     # --------------------------------------------------------------- pieces --
+    def _w(self, layer: int, key: str):
+        """Weight `key` of `layer` (-1: lm_head) in the layout the variant reads."""
+        wt = self.lm_head if layer < 0 else self.layers[layer][key]
+        if self.impl == "baseline":
+            return wt
+        pw = self._packed.get((layer, key))
+        if pw is None:
+            # gate|up rows interleaved in 64-row blocks for the SwiGLU epilogue
+            pw = self._packed[(layer, key)] = pack_weight(interleave_gate_up(wt) if key == "wgu" else wt)
+        return pw
+
     def _proj(self, x, wt, out):
         if self.impl == "baseline":
             out.copy_(F.linear(x, wt))
@@ -163,7 +188,7 @@ class LlamaTPDecoder:
         if self.world == 1:
             gemm(inp, wt, out=self.y)
             rmsnorm_residual(self.y, self.h, norm_w, eps, out=self.x)
-        elif self.B <= 32:
+        elif self.B * self.cfg.hidden * 2 <= self.comm.fused_bytes:
             gemm_allreduce_rmsnorm(self.comm, inp, wt, self.h, norm_w, eps, out=self.x)
         else:
             gemm(inp, wt, out=self.y)
@@ -175,16 +200,19 @@ class LlamaTPDecoder:
         torch.index_select(self.embed, 0, self.tokens, out=self.h)
         self.x.copy_(F.rms_norm(self.h, (cfg.hidden,), self.layers[0]["in_norm"], cfg.eps))
         for i, L in enumerate(self.layers):
-            self._proj(self.x, L["wqkv"], self.qkv)
+            self._proj(self.x, self._w(i, "wqkv"), self.qkv)
             ops.rope_append(self.qkv, self.cos, self.sin, self.pos, self.q, L["k"], L["v"], self.Hq, self.Hkv)
-            ops.decode_attention(self.q, L["k"], L["v"], self.pos, self.part_ml, self.part_o,
+            ops.decode_attention(self.q, L["k"], L["v"], self.pos, self.part_ml, self.part_o, self.attn_counters,
                                  self.attn.view(self.B, self.Hq, cfg.head_dim), self.splits)
-            self._row_parallel_tail(self.attn, L["wo"], L["post_norm"])
-            self._proj(self.x, L["wgu"], self.gu)
-            ops.silu_mul(self.gu, self.act)
+            self._row_parallel_tail(self.attn, self._w(i, "wo"), L["post_norm"])
+            if self.impl == "baseline":
+                self._proj(self.x, self._w(i, "wgu"), self.gu)
+                ops.silu_mul(self.gu, self.act)
+            else:
+                gemm_swiglu(self.x, self._w(i, "wgu"), out=self.act)
             nxt = self.layers[i + 1]["in_norm"] if i + 1 < len(self.layers) else self.final_norm
-            self._row_parallel_tail(self.act, L["wd"], nxt)
-        self._proj(self.x, self.lm_head, self.logits)
+            self._row_parallel_tail(self.act, self._w(i, "wd"), nxt)
+        self._proj(self.x, self._w(-1, "lm_head"), self.logits)
         val, idx = self.logits.float().max(dim=-1)
         if self.world > 1:
             mine = torch.stack([val, (idx + self.rank * self.v_local).float()], dim=-1).reshape(-1)

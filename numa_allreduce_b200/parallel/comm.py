@@ -147,6 +147,7 @@ class NumaAwareAllReduce:
         pipe_tile = pipe_tile if pipe_tile is not None else self.env.pipe_tile
         self._cfg = [oneshot_max, chunk_max, max_ctas, oneshot_ctas, fused_bytes, int(timeout), pipe_ctas,
                      pipe_tile]
+        self.fused_bytes = fused_bytes  # per-rank slot of the fused ops (GEMM + allreduce output)
         lay = ops.layout(self.world_size, self._cfg)
         self.workspace_bytes = int(lay[0])
         self.meta_ptrs = self._create_shared_buffer(self.workspace_bytes)

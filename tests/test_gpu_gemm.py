@@ -3,7 +3,7 @@
 import pytest
 import torch
 
-from numa_allreduce_b200.ops.gemm import gemm
+from numa_allreduce_b200.ops.gemm import gemm, gemm_swiglu, interleave_gate_up, pack_weight
 
 pytestmark = pytest.mark.gpu
 
@@ -49,3 +49,48 @@ def test_gemm_rejects_bad_shapes():
     wt = _rand((128, 100), 8, 0.02)
     with pytest.raises((RuntimeError, ValueError)):
         gemm(x, wt)
+
+
+def test_gemm_split_k_in_cuda_graph():
+    """A split-K launch (one cluster per tile) replays exactly from a CUDA graph."""
+    x = _rand((8, 3584), 9, 1.0)
+    wt = _rand((8192, 3584), 10, 0.02)
+    ref = x.float() @ wt.float().t()
+    out = torch.empty(8, 8192, dtype=torch.bfloat16, device="cuda")
+    gemm(x, wt, out=out, splits=4)  # first launch (attributes) outside capture
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        gemm(x, wt, out=out, splits=4)
+    for _ in range(3):
+        out.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
+    del g
+
+
+@pytest.mark.parametrize("T,N,K,splits", [(1, 1280, 8192, 0), (16, 512, 1024, 3), (200, 384, 640, 1)])
+def test_gemm_packed_weight(T, N, K, splits):
+    """The tiled weight layout gives the same product as the row-major one."""
+    x = _rand((T, K), 11, 1.0)
+    wt = _rand((N, K), 12, 0.02)
+    pw = pack_weight(wt)
+    assert torch.equal(pw.unpack(), wt)
+    y = gemm(x, pw, splits=splits)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(y.float(), x.float() @ wt.float().t(), rtol=2e-2, atol=2e-2)
+    assert torch.equal(y, gemm(x, wt, splits=splits))  # same split order, same bits
+
+
+@pytest.mark.parametrize("T,I,K,splits,packed", [(1, 3584, 1024, 0, True), (16, 256, 512, 3, False),
+                                                 (40, 128, 256, 1, True)])
+def test_gemm_swiglu_epilogue(T, I, K, splits, packed):
+    """silu(x @ gate.T) * (x @ up.T) from the interleaved gate|up weight."""
+    x = _rand((T, K), 13, 1.0)
+    wgu = _rand((2 * I, K), 14, 0.05)
+    w = interleave_gate_up(wgu)
+    y = gemm_swiglu(x, pack_weight(w) if packed else w, splits=splits)
+    h = x.float() @ wgu.float().t()
+    ref = torch.nn.functional.silu(h[:, :I]) * h[:, I:]
+    torch.cuda.synchronize()
+    torch.testing.assert_close(y.float(), ref, rtol=2e-2, atol=2e-2)

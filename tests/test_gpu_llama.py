@@ -13,8 +13,11 @@ from numa_allreduce_b200.ops import _ext
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("B,Hq,Hkv,L", [(1, 8, 1, 1025), (4, 16, 8, 300), (2, 8, 2, 64)])
-def test_decode_attention(B, Hq, Hkv, L):
+@pytest.mark.parametrize("B,Hq,Hkv,L,splits", [(1, 8, 1, 1025, 64), (4, 16, 8, 300, 5), (2, 8, 2, 64, 1),
+                                              (1, 8, 1, 3, 16), (3, 8, 1, 1025, 0)])
+def test_decode_attention(B, Hq, Hkv, L, splits):
+    """One launch: split partials and the combine by the last CTA; repeated
+    calls check that the arrival counters reset themselves."""
     ops = _ext.load()
     Lmax = ((L + 63) // 64) * 64
     g = torch.Generator(device="cuda").manual_seed(0)
@@ -22,13 +25,16 @@ def test_decode_attention(B, Hq, Hkv, L):
     k = torch.randn(B, Hkv, Lmax, 128, generator=g, device="cuda").to(torch.bfloat16)
     v = torch.randn(B, Hkv, Lmax, 128, generator=g, device="cuda").to(torch.bfloat16)
     pos = torch.tensor([L - 1], device="cuda", dtype=torch.int32)
-    splits = max(1, L // 64)
+    splits = splits or int(ops.attention_splits(B, Hkv, L))
     ml = torch.empty(B * Hq * splits * 2, device="cuda")
     po = torch.empty(B * Hq * splits * 128, device="cuda")
-    out = torch.empty(B, Hq, 128, device="cuda", dtype=torch.bfloat16)
-    ops.decode_attention(q, k, v, pos, ml, po, out, splits)
+    counters = torch.zeros(B * Hkv, device="cuda", dtype=torch.int32)
     ref = reference_attention(q, k, v, L)
-    torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
+    for _ in range(3):
+        out = torch.zeros(B, Hq, 128, device="cuda", dtype=torch.bfloat16)
+        ops.decode_attention(q, k, v, pos, ml, po, counters, out, splits)
+        torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
+    assert int(counters.abs().sum()) == 0
 
 
 def test_rope_append():

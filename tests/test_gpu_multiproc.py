@@ -142,7 +142,7 @@ def _worker_gemm_ar(rank, ws, port):
     """Fused row-parallel GEMM + allreduce + residual + RMSNorm (BASELINE
     config 4 shapes) against a PyTorch fp32 reference of the same layer."""
     from numa_allreduce_b200 import NumaAwareAllReduce
-    from numa_allreduce_b200.ops.gemm import gemm_allreduce_rmsnorm
+    from numa_allreduce_b200.ops.gemm import gemm_allreduce_rmsnorm, pack_weight
 
     _init(rank, ws, port)
     errors = []
@@ -158,10 +158,15 @@ def _worker_gemm_ar(rank, ws, port):
             gr = torch.Generator(device="cuda").manual_seed(77 + T)  # same residual on every rank
             res = torch.randn(T, H, generator=gr, device="cuda").to(torch.bfloat16)
             res0 = res.clone()
-            for rep in range(2):
-                res.copy_(res0)
-                out = gemm_allreduce_rmsnorm(ar, x, wt, res, norm_w, 1e-5)
-                torch.cuda.synchronize()
+            outs = []
+            pw = pack_weight(wt)
+            for splits in ((0, 1, 3) if T <= 16 else (0,)):  # auto, no split-K, an odd split count
+                for w_in in (wt, pw):
+                    for rep in range(2):
+                        res.copy_(res0)
+                        out = gemm_allreduce_rmsnorm(ar, x, w_in, res, norm_w, 1e-5, splits=splits)
+                        torch.cuda.synchronize()
+                    outs.append((splits, res.clone(), out.clone()))
             parts = (x.float() @ wt.float().t()).to(torch.bfloat16)  # each rank's partial, as the epilogue rounds it
             gathered = [torch.empty_like(parts) for _ in range(ws)]
             dist.all_gather(gathered, parts)
@@ -171,10 +176,12 @@ def _worker_gemm_ar(rank, ws, port):
             z = (acc + res0.float()).to(torch.bfloat16).float()
             ref = (z * torch.rsqrt(z.pow(2).mean(-1, keepdim=True) + 1e-5)).to(torch.bfloat16)
             # the reference GEMM accumulates in another order: allow a bf16 ulp of the partials
-            if not torch.allclose(res.float(), z, rtol=1e-2, atol=6e-2):
-                errors.append(f"T={T}: residual mismatch {(res.float() - z).abs().max().item()}")
-            if not torch.allclose(out.float(), ref.float(), rtol=2e-2, atol=2e-2):
-                errors.append(f"T={T}: output mismatch {(out.float() - ref.float()).abs().max().item()}")
+            for splits, res_k, out_k in outs:
+                if not torch.allclose(res_k.float(), z, rtol=1e-2, atol=6e-2):
+                    errors.append(f"T={T} splits={splits}: residual mismatch {(res_k.float() - z).abs().max().item()}")
+                if not torch.allclose(out_k.float(), ref.float(), rtol=2e-2, atol=2e-2):
+                    errors.append(f"T={T} splits={splits}: output mismatch "
+                                  f"{(out_k.float() - ref.float()).abs().max().item()}")
         try:
             ar.check()
         except Exception as e:
