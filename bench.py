@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Headline benchmark: bf16 allreduce across a sweep of message sizes.
 
-Metric (BASELINE.json): "bf16 allreduce p50 us & bus GB/s vs msg size at
+Metric: "bf16 allreduce p50 us & bus GB/s vs msg size at
 2/4/8 B200 vs ref & NCCL". One *step* is one out-of-place bf16 allreduce of
 each of 17 contiguous 1-D messages of 4 KiB .. 256 MiB (powers of two) per
 rank, N(0,1) data with seed = rank. ``value`` is the whole-job aggregate

@@ -1,5 +1,5 @@
 #!/usr/bin/env python3
-"""TP decode of a Llama-3-70B-shaped model in one CUDA graph (BASELINE config 5).
+"""TP decode of a Llama-3-70B-shaped model in one CUDA graph.
 
 hidden 8192, 80 layers, 64 q / 8 kv heads, head_dim 128, intermediate 28672,
 random N(0, 0.02) bf16 weights, synthetic KV cache with 1024 tokens of

@@ -85,9 +85,9 @@ def main():
     out = {"batch": a.batch, "layers": a.layers, "tp": a.tp, "impl": a.impl}
     variants = {
         "full": ([], False),
-        "no_attention": (["rope_append", "decode_attention"], False),
+        "no_attention": (["rope_append", "decode_attention", "rope_attention"], False),
         "no_norm": ([], True),
-        "gemm_only": (["rope_append", "decode_attention", "silu_mul"], True),
+        "gemm_only": (["rope_append", "decode_attention", "rope_attention", "silu_mul"], True),
     }
     for name, (skip, no_norm) in variants.items():
         model.ops = _Skip(real_ops, skip)

@@ -1,5 +1,5 @@
 #!/usr/bin/env python3
-"""Fused TP layer tail (BASELINE config 4): row-parallel GEMM -> allreduce ->
+"""Fused TP layer tail: row-parallel GEMM -> allreduce ->
 residual add -> RMSNorm, Llama-3-8B shapes at TP = world size.
 
 Per rank: activations [T, 1792] ~ N(0,1), down_proj weight [1792, 4096] ~
@@ -7,11 +7,12 @@ N(0, 0.02) (stored as [4096, 1792], K-major), residual [T, 4096] ~ N(0,1),
 RMSNorm eps 1e-5 with weight ones, T in {1, 16, 128, 512}. Variants:
 
   baseline   cuBLAS GEMM (torch.matmul) + NCCL all_reduce + residual add +
-             torch RMSNorm (the unfused stack the BASELINE names)
+             torch RMSNorm (the unfused stack)
   fused      this library: tcgen05 GEMM whose epilogue stores partial tiles
              into every rank over NVLink, then rank-order sum + residual +
              RMSNorm (two launches)
   lib_unfused  this library's tcgen05 GEMM + fused allreduce/norm kernel
+  cublas_fused_ar  cuBLAS GEMM + this library's fused allreduce/norm kernel
 
 Each variant's per-layer time is measured by capturing `--graph-calls` layer
 tails in one CUDA graph (NCCL included) and timing replays; weights rotate
@@ -37,7 +38,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path.insert(0, ROOT)
 
 from numa_allreduce_b200 import NumaAwareAllReduce, fused_allreduce_rmsnorm  # noqa: E402
-from numa_allreduce_b200.ops.gemm import gemm, gemm_allreduce_rmsnorm  # noqa: E402
+from numa_allreduce_b200.ops.gemm import gemm, gemm_allreduce_rmsnorm, pack_weight  # noqa: E402
 
 
 def parse():
@@ -93,6 +94,7 @@ def main():
     copies = max(1, (256 << 20) // (H * K * 2))  # > L2: weights come from HBM
     wts = [(torch.randn(H, K, generator=g, device="cuda") * 0.02).to(torch.bfloat16) for _ in range(copies)]
     w_kn = [w.t().contiguous() for w in wts]  # [K, H] for the cuBLAS baseline (x @ W)
+    wps = [pack_weight(w) for w in wts]  # tiled layout read by this library's GEMM
     norm_w = torch.ones(H, device="cuda", dtype=torch.bfloat16)
     rows = []
     for T in [int(t) for t in args.tokens.split(",")]:
@@ -109,10 +111,14 @@ def main():
             out.copy_(F.rms_norm(res, (H,), norm_w, 1e-5))
 
         def fused(i):
-            gemm_allreduce_rmsnorm(ar, x, wts[i % copies], res, norm_w, 1e-5, out=out)
+            gemm_allreduce_rmsnorm(ar, x, wps[i % copies], res, norm_w, 1e-5, out=out)
 
         def lib_unfused(i):
-            gemm(x, wts[i % copies], out=y)
+            gemm(x, wps[i % copies], out=y)
+            fused_allreduce_rmsnorm(ar, y, res, norm_w, 1e-5, out=out)
+
+        def cublas_fused_ar(i):
+            torch.matmul(x, w_kn[i % copies], out=y)
             fused_allreduce_rmsnorm(ar, y, res, norm_w, 1e-5, out=out)
 
         # correctness of the fused path against the baseline on the same inputs
@@ -125,7 +131,8 @@ def main():
         err = (out.float() - ref.float()).abs().max().item()
         res.copy_(r0)
         row = {"T": T, "world_size": world, "max_abs_diff_vs_baseline": err}
-        for name, fn in (("baseline", baseline), ("fused", fused), ("lib_unfused", lib_unfused)):
+        for name, fn in (("baseline", baseline), ("fused", fused), ("lib_unfused", lib_unfused),
+                         ("cublas_fused_ar", cublas_fused_ar)):
             row[name + "_us"] = round(timed_graph(fn, args.graph_calls, args.reps), 2)
             res.copy_(r0)
         row["speedup_fused_vs_baseline"] = round(row["baseline_us"] / row["fused_us"], 3)

@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Allreduce sweep: p50 latency and bus bandwidth per protocol, dtype and size.
 
-BASELINE configs 2 and 3: contiguous 1-D tensors of 4 KiB .. 256 MiB (powers
+Contiguous 1-D tensors of 4 KiB .. 256 MiB (powers
 of two), N(0,1) with seed = rank, every protocol of this library plus NCCL and
 the reference's custom allreduce (``--ref``), 200 timed iterations after 20
 warm-up. Launch with torch.distributed.run, one process per GPU::

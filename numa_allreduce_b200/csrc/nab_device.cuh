@@ -171,6 +171,9 @@ NAB_DINLINE void st_volatile_u32(uint32_t* p, uint32_t v) {
 // programmatic stream serialization begin scheduling now (it waits for this
 // grid's completion before it reads anything this grid writes).
 NAB_DINLINE void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// Waits for the grids this launch programmatically depends on to complete
+// (no-op without such a dependency).
+NAB_DINLINE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 NAB_DINLINE uint64_t globaltimer_ns() {
   uint64_t t;

@@ -115,6 +115,7 @@ template <int PPT>
 __global__ void __launch_bounds__(kFThreads) k_rmsnorm(const uint4* __restrict__ in, uint4* residual,
                                                        const uint4* __restrict__ w, uint4* out, int T,
                                                        int H, float eps) {
+  pdl_wait();
   pdl_trigger();
   const int hp = H / 8;
   for (int t = blockIdx.x; t < T; t += gridDim.x) {
@@ -279,6 +280,7 @@ __global__ void __launch_bounds__(kFThreads) k_slots_rmsnorm(const char* base, i
                                                              int ws, int tile_tokens, int m_tiles, WaitCtx w,
                                                              uint4* residual, const uint4* wgt, uint4* out, int T,
                                                              int H, float eps) {
+  pdl_wait();
   pdl_trigger();
   const SignalPad* pad = reinterpret_cast<const SignalPad*>(base);
   const uint32_t epoch = ld_volatile_u32(&pad->epoch);
@@ -418,6 +420,24 @@ FusedView make_view(const Communicator& c, const void* in, void* residual, const
   return v;
 }
 
+// Launch as a programmatic dependent launch: the CTAs become resident while
+// the kernel before is still running and start at its completion
+// (griddepcontrol.wait at the top of the kernel).
+template <typename... KArgs, typename... Args>
+void launch_pdl(void (*kernel)(KArgs...), int grid, int block, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.stream = s;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+  if (e != cudaSuccess) throw std::runtime_error(std::string("norm launch failed: ") + cudaGetErrorString(e));
+}
+
 void check_ptrs(const void* a, const void* b, const void* c, const void* d) {
   for (const void* x : {a, b, c, d})
     if (reinterpret_cast<uintptr_t>(x) % 16 != 0) throw std::invalid_argument("fused rmsnorm: 16-byte alignment");
@@ -447,10 +467,10 @@ void slots_rmsnorm(Communicator& c, cudaStream_t s, void* residual, const void* 
   const int t = static_cast<int>(T), h = static_cast<int>(H), ws = c.world_size();
   const int m_tiles = h / 128;
   switch (ppt_for(H)) {
-    case 1: k_slots_rmsnorm<1><<<grid, kFThreads, 0, s>>>(base, L.fused_off, L.fused_bytes, ws, tile_tokens, m_tiles, w, r4, w4, o4, t, h, eps); break;
-    case 2: k_slots_rmsnorm<2><<<grid, kFThreads, 0, s>>>(base, L.fused_off, L.fused_bytes, ws, tile_tokens, m_tiles, w, r4, w4, o4, t, h, eps); break;
-    case 4: k_slots_rmsnorm<4><<<grid, kFThreads, 0, s>>>(base, L.fused_off, L.fused_bytes, ws, tile_tokens, m_tiles, w, r4, w4, o4, t, h, eps); break;
-    default: k_slots_rmsnorm<8><<<grid, kFThreads, 0, s>>>(base, L.fused_off, L.fused_bytes, ws, tile_tokens, m_tiles, w, r4, w4, o4, t, h, eps); break;
+    case 1: launch_pdl(k_slots_rmsnorm<1>, grid, kFThreads, s, base, L.fused_off, L.fused_bytes, ws, tile_tokens, m_tiles, w, r4, w4, o4, t, h, eps); break;
+    case 2: launch_pdl(k_slots_rmsnorm<2>, grid, kFThreads, s, base, L.fused_off, L.fused_bytes, ws, tile_tokens, m_tiles, w, r4, w4, o4, t, h, eps); break;
+    case 4: launch_pdl(k_slots_rmsnorm<4>, grid, kFThreads, s, base, L.fused_off, L.fused_bytes, ws, tile_tokens, m_tiles, w, r4, w4, o4, t, h, eps); break;
+    default: launch_pdl(k_slots_rmsnorm<8>, grid, kFThreads, s, base, L.fused_off, L.fused_bytes, ws, tile_tokens, m_tiles, w, r4, w4, o4, t, h, eps); break;
   }
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string("slots rmsnorm launch failed: ") + cudaGetErrorString(e));
@@ -468,10 +488,10 @@ void rmsnorm_residual(cudaStream_t s, const void* inp, void* residual, const voi
   auto* o4 = static_cast<uint4*>(out);
   const int t = static_cast<int>(T), h = static_cast<int>(H);
   switch (ppt_for(H)) {
-    case 1: k_rmsnorm<1><<<grid, kFThreads, 0, s>>>(i4, r4, w4, o4, t, h, eps); break;
-    case 2: k_rmsnorm<2><<<grid, kFThreads, 0, s>>>(i4, r4, w4, o4, t, h, eps); break;
-    case 4: k_rmsnorm<4><<<grid, kFThreads, 0, s>>>(i4, r4, w4, o4, t, h, eps); break;
-    default: k_rmsnorm<8><<<grid, kFThreads, 0, s>>>(i4, r4, w4, o4, t, h, eps); break;
+    case 1: launch_pdl(k_rmsnorm<1>, grid, kFThreads, s, i4, r4, w4, o4, t, h, eps); break;
+    case 2: launch_pdl(k_rmsnorm<2>, grid, kFThreads, s, i4, r4, w4, o4, t, h, eps); break;
+    case 4: launch_pdl(k_rmsnorm<4>, grid, kFThreads, s, i4, r4, w4, o4, t, h, eps); break;
+    default: launch_pdl(k_rmsnorm<8>, grid, kFThreads, s, i4, r4, w4, o4, t, h, eps); break;
   }
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string("rmsnorm launch failed: ") + cudaGetErrorString(e));

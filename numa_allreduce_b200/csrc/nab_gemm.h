@@ -17,6 +17,10 @@ namespace nab {
 // packed: wt is in the tiled layout of pack_weight_tiles — [N/128][K/64] tiles
 // of 128 rows x 64 columns, each 16 KB contiguous — so every weight TMA load
 // reads one contiguous block of HBM instead of 128 rows 2K bytes apart.
+// Launched as a programmatic dependent launch: the weight loads may start
+// while the kernel before it in the stream still runs, if that kernel is one
+// of this library's (they allow early launch); such a kernel must not write
+// wt. Activations are read only after it completed.
 // swiglu: every 128-row tile of wt holds 64 gate rows followed by the 64
 // matching up rows (interleave_gate_up); y is then [T, N/2] with
 // y = silu(gate) * up computed from the fp32 accumulators.

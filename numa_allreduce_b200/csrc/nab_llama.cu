@@ -18,14 +18,18 @@
 #include <string>
 
 #include "nab_device.cuh"
+#include "nab_driver.h"
 #include "nab_llama.h"
+#include "nab_sm100.cuh"
 
 namespace nab {
 
 namespace {
 
 constexpr int kHeadDim = 128;
-constexpr int kChunk = 64;  // positions per attention split
+constexpr int kChunk = 64;           // K/V rows staged per step
+constexpr int kMaxAttnSplits = 16;  // CTAs per (batch, kv head): one cluster
+constexpr int kAttnSmem = 2 * 2 * kChunk * kHeadDim * 2;  // 2 stages of K and V chunks
 
 NAB_DINLINE float bf2f(__nv_bfloat16 v) { return __bfloat162float(v); }
 
@@ -58,140 +62,279 @@ __global__ void k_rope_append(const __nv_bfloat16* __restrict__ qkv, const float
   }
 }
 
-// grid (B, Hkv, splits), block 32 * G threads (G = Hq / Hkv query heads per
-// kv head, one warp each). Each CTA covers one contiguous range of positions:
-// K/V rows are staged in shared memory 64 at a time, every warp scores four
-// positions per step (four independent shuffle reductions in flight) and
-// keeps an online softmax (running max m, sum l, unnormalised output).
-// The partial (m, l, o) of every (b, head, split) goes to scratch; the last
-// CTA of a (b, kv head) to finish (arrival counter, reset by that CTA) combines
-// the splits of its G heads and writes the output, so one launch does both.
-__global__ void __launch_bounds__(256) k_attn_decode(const __nv_bfloat16* __restrict__ q,
-                                                     const __nv_bfloat16* __restrict__ k_cache,
-                                                     const __nv_bfloat16* __restrict__ v_cache,
-                                                     const int* __restrict__ pos_ptr, float* __restrict__ part_ml,
-                                                     float* __restrict__ part_o, int* __restrict__ counters,
-                                                     __nv_bfloat16* __restrict__ out, int Hq, int Hkv, int Lmax,
-                                                     int splits, float scale) {
-  pdl_trigger();
-  __shared__ __align__(16) __nv_bfloat16 sk[kChunk][kHeadDim + 8];
-  __shared__ __align__(16) __nv_bfloat16 sv[kChunk][kHeadDim + 8];
-  __shared__ int s_last;
-  const int b = blockIdx.x, kvh = blockIdx.y, sp = blockIdx.z;
-  const int G = Hq / Hkv;
+struct AttnArgs {
+  const __nv_bfloat16* q;  // [B, q_stride]: q heads at 0 (kRope: the qkv projection)
+  const float* cos_t;      // kRope: [Lmax, 64]
+  const float* sin_t;
+  const int* pos;          // position being decoded (device memory)
+  __nv_bfloat16* k_cache;  // [B, Hkv, Lmax, 128]
+  __nv_bfloat16* v_cache;
+  __nv_bfloat16* out;      // [B, Hq, 128]
+  int q_stride;
+  int Hq, Hkv, Lmax, splits;
+  float scale;
+};
+
+NAB_DINLINE uint2 pack4(const float (&f)[4]) {
+  __nv_bfloat162 a0 = __floats2bfloat162_rn(f[0], f[1]), a1 = __floats2bfloat162_rn(f[2], f[3]);
+  uint2 r;
+  r.x = *reinterpret_cast<uint32_t*>(&a0);
+  r.y = *reinterpret_cast<uint32_t*>(&a1);
+  return r;
+}
+
+// GQA decode attention. grid (splits, B * Hkv); the `splits` CTAs of one
+// (batch, kv head) form a thread-block cluster and each covers one
+// contiguous range of positions. Block: one warp per query head of the group
+// (G = Hq / Hkv <= 8); lane l holds dims 4l..4l+3. K/V rows of the range are
+// contiguous in the cache, so each 64-row chunk arrives by two bulk copies
+// (TMA) into a 2-stage shared-memory ring while the previous chunk is
+// scored; every warp scores four positions per step (four independent
+// shuffle reductions in flight) with an online softmax (running max m, sum
+// l, unnormalised output). Each CTA leaves its partial in shared memory;
+// after a cluster barrier CTA 0 combines the splits over distributed shared
+// memory and writes the output: one launch, no scratch.
+// kRope: q and the new k are rotated here from the qkv projection; the CTA
+// holding the current position writes k and v to the cache and into its
+// staged chunk.
+template <bool kRope>
+__global__ void __launch_bounds__(256) k_attn(const __grid_constant__ AttnArgs a) {
+  extern __shared__ __align__(128) uint8_t attn_smem[];
+  // [stage][K | V][kChunk][kHeadDim] bf16
+  auto kv_tile = [&](int stage, int which) {
+    return reinterpret_cast<__nv_bfloat16*>(attn_smem) + (stage * 2 + which) * kChunk * kHeadDim;
+  };
+  __shared__ __align__(16) float s_o[8][kHeadDim];
+  __shared__ float s_m[8], s_l[8];
+  __shared__ __align__(8) uint64_t full_bar[2];
+  __shared__ int s_abort;
+  volatile int* abort_flag = &s_abort;
+  const int sp = blockIdx.x, b = blockIdx.y / a.Hkv, kvh = blockIdx.y % a.Hkv;
+  const int G = a.Hq / a.Hkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = kvh * G + warp;
-  const int L = *pos_ptr + 1;
-  const int per = (L + splits - 1) / splits;
-  const int beg = sp * per, end = min(L, beg + per);
-  // q of this warp's head: lane holds dims lane*4 .. lane*4+3
-  float qv[4];
-  {
-    const uint2 raw = *reinterpret_cast<const uint2*>(q + (static_cast<int64_t>(b) * Hq + h) * kHeadDim + lane * 4);
-    const __nv_bfloat162 q01 = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
-    const __nv_bfloat162 q23 = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
-    qv[0] = __low2float(q01) * scale;
-    qv[1] = __high2float(q01) * scale;
-    qv[2] = __low2float(q23) * scale;
-    qv[3] = __high2float(q23) * scale;
+  if (threadIdx.x == 0) {
+    sm100::mbar_init(&full_bar[0], 1);
+    sm100::mbar_init(&full_bar[1], 1);
+    sm100::fence_barrier_init();
+    s_abort = 0;
   }
-  float m = -INFINITY, l = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
-  const __nv_bfloat16* kb = k_cache + (static_cast<int64_t>(b) * Hkv + kvh) * Lmax * kHeadDim;
-  const __nv_bfloat16* vb = v_cache + (static_cast<int64_t>(b) * Hkv + kvh) * Lmax * kHeadDim;
-  auto row4 = [&](const __nv_bfloat16* r, float (&f)[4]) {
-    const uint2 raw = *reinterpret_cast<const uint2*>(r + lane * 4);
-    const __nv_bfloat162 a0 = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
-    const __nv_bfloat162 a1 = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
-    f[0] = __low2float(a0);
-    f[1] = __high2float(a0);
-    f[2] = __low2float(a1);
-    f[3] = __high2float(a1);
+  __syncthreads();
+  sm100::griddep_wait();  // inputs come from the kernel before (programmatic launch)
+  pdl_trigger();
+  const int pos = *a.pos;
+  const int L = pos + 1;
+  const int per = (L + a.splits - 1) / a.splits;
+  const int beg = sp * per, end = min(L, beg + per);
+  const int nchunks = end > beg ? (end - beg + kChunk - 1) / kChunk : 0;
+  const int64_t kv_base = (static_cast<int64_t>(b) * a.Hkv + kvh) * a.Lmax * kHeadDim;
+  const __nv_bfloat16* kb = a.k_cache + kv_base;
+  const __nv_bfloat16* vb = a.v_cache + kv_base;
+  int issued = 0;  // chunks whose copies thread 0 started
+  auto issue = [&](int i) {  // chunk i into stage i & 1 (thread 0)
+    ++issued;
+    const int c0 = beg + i * kChunk, n = min(kChunk, end - c0);
+    const uint32_t bytes = static_cast<uint32_t>(n) * kHeadDim * 2;
+    sm100::mbar_arrive_expect_tx(&full_bar[i & 1], 2 * bytes);
+    sm100::bulk_load(kv_tile(i & 1, 0), kb + static_cast<int64_t>(c0) * kHeadDim, bytes, &full_bar[i & 1]);
+    sm100::bulk_load(kv_tile(i & 1, 1), vb + static_cast<int64_t>(c0) * kHeadDim, bytes, &full_bar[i & 1]);
   };
-  for (int c0 = beg; c0 < end; c0 += kChunk) {
-    const int n = min(kChunk, end - c0);
-    __syncthreads();
-    for (int idx = threadIdx.x; idx < n * (kHeadDim / 8); idx += blockDim.x) {
-      const int r = idx / (kHeadDim / 8), cc = (idx % (kHeadDim / 8)) * 8;
-      *reinterpret_cast<uint4*>(&sk[r][cc]) = *reinterpret_cast<const uint4*>(kb + static_cast<int64_t>(c0 + r) * kHeadDim + cc);
-      *reinterpret_cast<uint4*>(&sv[r][cc]) = *reinterpret_cast<const uint4*>(vb + static_cast<int64_t>(c0 + r) * kHeadDim + cc);
+  if (threadIdx.x == 0)
+    for (int i = 0; i < min(2, nchunks); ++i) issue(i);
+
+  // Lane = (group g = lane / 8, slice s = lane % 8). Group g scores the
+  // positions j + g of each step of 4; slice s holds dims 8s..8s+7 and
+  // 64+8s..64+8s+7 (a rotary pair sits in one lane; the 8 lanes of a group
+  // read one contiguous 256-byte K/V row without bank conflicts).
+  const int g = lane >> 3, sl = lane & 7;
+  const int d0 = 8 * sl, d1 = 64 + 8 * sl;
+  const __nv_bfloat16* qrow = a.q + static_cast<int64_t>(b) * a.q_stride;
+  auto load8 = [](const __nv_bfloat16* p, float* f) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      f[2 * k] = __uint_as_float(w[k] << 16);
+      f[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
+    }
+  };
+  auto store8 = [](__nv_bfloat16* p, const float* f) {
+    uint4 r;
+    uint32_t* w = reinterpret_cast<uint32_t*>(&r);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      __nv_bfloat162 t = __floats2bfloat162_rn(f[2 * k], f[2 * k + 1]);
+      w[k] = *reinterpret_cast<uint32_t*>(&t);
+    }
+    *reinterpret_cast<uint4*>(p) = r;
+  };
+  // half-split rotary embedding of dims (d0 + e, d1 + e), both in this lane
+  auto rope16 = [&](float* x) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float c = a.cos_t[pos * (kHeadDim / 2) + d0 + e], sn = a.sin_t[pos * (kHeadDim / 2) + d0 + e];
+      const float x1 = x[e], x2 = x[8 + e];
+      x[e] = x1 * c - x2 * sn;
+      x[8 + e] = x2 * c + x1 * sn;
+    }
+  };
+  float qv[16];
+  if (warp < G) {
+    load8(qrow + h * kHeadDim + d0, qv);
+    load8(qrow + h * kHeadDim + d1, qv + 8);
+    if (kRope) {
+      rope16(qv);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) qv[e] = __bfloat162float(__float2bfloat16_rn(qv[e]));  // as rope_append stores q
+    }
+#pragma unroll
+    for (int e = 0; e < 16; ++e) qv[e] *= a.scale;
+  }
+  // the new position's k (rotated) and v: to the cache, and into the staged
+  // chunk below (the bulk copy may have read the row before this store);
+  // lanes 0-7 of warp 0 hold them
+  const bool owns_pos = kRope && beg <= pos && pos < end;
+  float k_new[16], v_new[16];
+  if (owns_pos && warp == 0 && g == 0) {
+    load8(qrow + (a.Hq + kvh) * kHeadDim + d0, k_new);
+    load8(qrow + (a.Hq + kvh) * kHeadDim + d1, k_new + 8);
+    rope16(k_new);
+    load8(qrow + (a.Hq + a.Hkv + kvh) * kHeadDim + d0, v_new);
+    load8(qrow + (a.Hq + a.Hkv + kvh) * kHeadDim + d1, v_new + 8);
+    const int64_t at = kv_base + static_cast<int64_t>(pos) * kHeadDim;
+    store8(a.k_cache + at + d0, k_new);
+    store8(a.k_cache + at + d1, k_new + 8);
+    store8(a.v_cache + at + d0, v_new);
+    store8(a.v_cache + at + d1, v_new + 8);
+  }
+
+  float m = -INFINITY, l = 0.f, acc[16];
+#pragma unroll
+  for (int e = 0; e < 16; ++e) acc[e] = 0.f;
+  // one position of this group: score, then the online-softmax update
+  auto score = [&](const __nv_bfloat16* krow) {
+    float kf[16];
+    load8(krow + d0, kf);
+    load8(krow + d1, kf + 8);
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+    for (int e = 0; e < 16; e += 4) {
+      s0 += qv[e] * kf[e];
+      s1 += qv[e + 1] * kf[e + 1];
+      s2 += qv[e + 2] * kf[e + 2];
+      s3 += qv[e + 3] * kf[e + 3];
+    }
+    return (s0 + s1) + (s2 + s3);
+  };
+  auto update = [&](float d, const __nv_bfloat16* vrow) {
+    float vf[16];
+    load8(vrow + d0, vf);
+    load8(vrow + d1, vf + 8);
+    const float mn = fmaxf(m, d);
+    const float corr = __expf(m - mn), p = __expf(d - mn);
+    l = l * corr + p;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) acc[e] = acc[e] * corr + p * vf[e];
+    m = mn;
+  };
+  int consumed = 0;
+  for (int i = 0; i < nchunks; ++i) {
+    const int c0 = beg + i * kChunk, n = min(kChunk, end - c0);
+    if (!sm100::mbar_wait(&full_bar[i & 1], (i >> 1) & 1, 1000000000ull, abort_flag)) *abort_flag = 1;
+    else consumed = i + 1;
+    const __nv_bfloat16* sk = kv_tile(i & 1, 0);
+    const __nv_bfloat16* sv = kv_tile(i & 1, 1);
+    if (owns_pos && warp == 0 && g == 0 && pos >= c0 && pos < c0 + n) {
+      store8(kv_tile(i & 1, 0) + (pos - c0) * kHeadDim + d0, k_new);
+      store8(kv_tile(i & 1, 0) + (pos - c0) * kHeadDim + d1, k_new + 8);
+      store8(kv_tile(i & 1, 1) + (pos - c0) * kHeadDim + d0, v_new);
+      store8(kv_tile(i & 1, 1) + (pos - c0) * kHeadDim + d1, v_new + 8);
     }
     __syncthreads();
+    if (*abort_flag) break;
     if (warp < G) {
-      for (int j = 0; j < n; j += 4) {
-        float d[4];
+      // two positions of this group per iteration, both scores first; the
+      // trip count is the same for every lane (the shuffles need the whole
+      // warp), positions past the chunk are scored on a valid row and skipped
+      for (int j0 = 0; j0 < n; j0 += 8) {
+        const int ja = j0 + g, jb = j0 + 4 + g;
+        float da = score(sk + min(ja, n - 1) * kHeadDim), db = score(sk + min(jb, n - 1) * kHeadDim);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          float kf[4];
-          row4(sk[min(j + u, n - 1)], kf);
-          d[u] = qv[0] * kf[0] + qv[1] * kf[1] + qv[2] * kf[2] + qv[3] * kf[3];
+        for (int o = 1; o < 8; o <<= 1) {
+          da += __shfl_xor_sync(0xffffffffu, da, o);
+          db += __shfl_xor_sync(0xffffffffu, db, o);
         }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-          for (int u = 0; u < 4; ++u) d[u] += __shfl_xor_sync(0xffffffffu, d[u], o);
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-          if (j + u >= n) d[u] = -INFINITY;
-        const float mn = fmaxf(fmaxf(m, fmaxf(d[0], d[1])), fmaxf(d[2], d[3]));
-        const float corr = __expf(m - mn);
-        float p[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) p[u] = __expf(d[u] - mn);
-        l = l * corr + ((p[0] + p[1]) + (p[2] + p[3]));
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[e] *= corr;
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          float vf[4];
-          row4(sv[min(j + u, n - 1)], vf);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) acc[e] += p[u] * vf[e];
-        }
-        m = mn;
+        if (ja < n) update(da, sv + ja * kHeadDim);
+        if (jb < n) update(db, sv + jb * kHeadDim);
       }
     }
+    __syncthreads();  // every warp is done with this stage
+    if (threadIdx.x == 0 && i + 2 < nchunks) issue(i + 2);
   }
+  if (*abort_flag && threadIdx.x == 0) {
+    // let copies still in flight land before the CTA's memory goes away
+    volatile int never = 0;
+    for (int i = consumed; i < issued; ++i) sm100::mbar_wait(&full_bar[i & 1], (i >> 1) & 1, 1000000000ull, &never);
+  }
+  // merge the four groups' running states (xor 8, then 16)
   if (warp < G) {
-    const int64_t idx = (static_cast<int64_t>(b) * Hq + h) * splits + sp;
-    if (lane == 0) {
-      part_ml[idx * 2] = m;
-      part_ml[idx * 2 + 1] = l;
+#pragma unroll
+    for (int o = 8; o < 32; o <<= 1) {
+      const float m_o = __shfl_xor_sync(0xffffffffu, m, o);
+      const float l_o = __shfl_xor_sync(0xffffffffu, l, o);
+      const float mn = fmaxf(m, m_o);
+      const float w_me = m == -INFINITY ? 0.f : __expf(m - mn);
+      const float w_o = m_o == -INFINITY ? 0.f : __expf(m_o - mn);
+      l = l * w_me + l_o * w_o;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) acc[e] = acc[e] * w_me + __shfl_xor_sync(0xffffffffu, acc[e], o) * w_o;
+      m = mn;
     }
-    *reinterpret_cast<float4*>(part_o + idx * kHeadDim + lane * 4) = make_float4(acc[0], acc[1], acc[2], acc[3]);
   }
-  // last split CTA of this (b, kv head) combines
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int* ctr = counters + b * Hkv + kvh;
-    s_last = atomicAdd(ctr, 1) == splits - 1;
-    if (s_last) *ctr = 0;
+  if (warp < G && g == 0) {
+    if (lane == 0) {
+      s_m[warp] = m;
+      s_l[warp] = l;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      s_o[warp][d0 + e] = acc[e];
+      s_o[warp][d1 + e] = acc[8 + e];
+    }
   }
-  __syncthreads();
-  if (!s_last || warp >= G) return;
-  __threadfence();
-  const int64_t base = (static_cast<int64_t>(b) * Hq + h) * splits;
-  float M = -INFINITY;
-  for (int s2 = 0; s2 < splits; ++s2) M = fmaxf(M, __ldcg(part_ml + (base + s2) * 2));
-  float den = 0.f, num[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int s2 = 0; s2 < splits; ++s2) {
-    const float ms = __ldcg(part_ml + (base + s2) * 2);
-    if (ms == -INFINITY) continue;
-    const float w = __expf(ms - M);
-    den += w * __ldcg(part_ml + (base + s2) * 2 + 1);
-    const float4 o = __ldcg(reinterpret_cast<const float4*>(part_o + (base + s2) * kHeadDim + lane * 4));
-    num[0] += w * o.x;
-    num[1] += w * o.y;
-    num[2] += w * o.z;
-    num[3] += w * o.w;
+  if (a.splits > 1) sm100::cluster_sync(); else __syncthreads();
+  if (sp == 0 && warp < G) {
+    // lane s reads split s's (m, l); weights exp(m_s - M), in split order
+    const uint32_t m_addr = sm100::smem_u32(&s_m[warp]), l_addr = sm100::smem_u32(&s_l[warp]);
+    const uint32_t o_addr = sm100::smem_u32(&s_o[warp][lane * 4]);
+    float ms = -INFINITY, ls = 0.f;
+    if (lane < a.splits) {
+      ms = a.splits > 1 ? sm100::ld_dsmem_f32(sm100::dsmem_addr(m_addr, lane)) : s_m[warp];
+      ls = a.splits > 1 ? sm100::ld_dsmem_f32(sm100::dsmem_addr(l_addr, lane)) : s_l[warp];
+    }
+    float M = ms;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    const float wgt = ms == -INFINITY ? 0.f : __expf(ms - M);
+    float den = wgt * ls;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+    float num[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int s2 = 0; s2 < a.splits; ++s2) {
+      const float w = __shfl_sync(0xffffffffu, wgt, s2);
+      if (w == 0.f) continue;
+      const float4 o = a.splits > 1 ? sm100::ld_dsmem_f4(sm100::dsmem_addr(o_addr, s2))
+                                    : *reinterpret_cast<const float4*>(&s_o[warp][lane * 4]);
+      num[0] += w * o.x;
+      num[1] += w * o.y;
+      num[2] += w * o.z;
+      num[3] += w * o.w;
+    }
+    const float inv = 1.f / den;
+    const float r[4] = {num[0] * inv, num[1] * inv, num[2] * inv, num[3] * inv};
+    *reinterpret_cast<uint2*>(a.out + (static_cast<int64_t>(b) * a.Hq + h) * kHeadDim + lane * 4) = pack4(r);
   }
-  const float inv = 1.f / den;
-  __nv_bfloat162 o01 = __floats2bfloat162_rn(num[0] * inv, num[1] * inv);
-  __nv_bfloat162 o23 = __floats2bfloat162_rn(num[2] * inv, num[3] * inv);
-  uint2 packed;
-  packed.x = *reinterpret_cast<uint32_t*>(&o01);
-  packed.y = *reinterpret_cast<uint32_t*>(&o23);
-  *reinterpret_cast<uint2*>(out + (static_cast<int64_t>(b) * Hq + h) * kHeadDim + lane * 4) = packed;
+  if (a.splits > 1) sm100::cluster_sync();  // CTA 0 has read every partial
 }
 
 // out[b, i] = silu(gu[b, i]) * gu[b, I + i]
@@ -221,23 +364,90 @@ void rope_append(cudaStream_t s, const void* qkv, const float* cos_t, const floa
   check("rope_append");
 }
 
+namespace {
+
+template <bool kRope>
+void launch_attn(cudaStream_t s, const AttnArgs& a, int B) {
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    NAB_CUDA_CHECK(cudaFuncSetAttribute(k_attn<kRope>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    NAB_CUDA_CHECK(cudaFuncSetAttribute(k_attn<kRope>, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem));
+    attr_set[dev & 63] = true;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(a.splits, B * a.Hkv);
+  cfg.blockDim = dim3(32 * (a.Hq / a.Hkv));
+  cfg.dynamicSmemBytes = kAttnSmem;
+  cfg.stream = s;
+  cudaLaunchAttribute attrs[2];
+  attrs[0].id = cudaLaunchAttributeClusterDimension;
+  attrs[0].val.clusterDim.x = a.splits;
+  attrs[0].val.clusterDim.y = 1;
+  attrs[0].val.clusterDim.z = 1;
+  attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = 2;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, k_attn<kRope>, a);
+  if (e != cudaSuccess) throw std::runtime_error(std::string("attention launch failed: ") + cudaGetErrorString(e));
+}
+
+void check_attn(int Hq, int Hkv, int splits) {
+  if (Hkv < 1 || Hq % Hkv != 0 || Hq / Hkv > 8) throw std::invalid_argument("attention: need Hq / Hkv <= 8");
+  if (splits < 1 || splits > kMaxAttnSplits) throw std::invalid_argument("attention: splits must be in [1, 16]");
+}
+
+}  // namespace
+
 void decode_attention(cudaStream_t s, const void* q, const void* k_cache, const void* v_cache, const int* pos,
-                      float* part_ml, float* part_o, int* counters, void* out, int B, int Hq, int Hkv, int Lmax,
-                      int splits) {
-  if (Hq % Hkv != 0 || Hq / Hkv > 8) throw std::invalid_argument("attention: need Hq / Hkv <= 8");
-  const float scale = 1.f / sqrtf(static_cast<float>(kHeadDim));
-  k_attn_decode<<<dim3(B, Hkv, splits), 32 * (Hq / Hkv), 0, s>>>(
-      static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k_cache),
-      static_cast<const __nv_bfloat16*>(v_cache), pos, part_ml, part_o, counters,
-      static_cast<__nv_bfloat16*>(out), Hq, Hkv, Lmax, splits, scale);
-  check("attention");
+                      void* out, int B, int Hq, int Hkv, int Lmax, int splits) {
+  check_attn(Hq, Hkv, splits);
+  AttnArgs a{};
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.pos = pos;
+  a.k_cache = static_cast<__nv_bfloat16*>(const_cast<void*>(k_cache));
+  a.v_cache = static_cast<__nv_bfloat16*>(const_cast<void*>(v_cache));
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.q_stride = Hq * kHeadDim;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.Lmax = Lmax;
+  a.splits = splits;
+  a.scale = 1.f / sqrtf(static_cast<float>(kHeadDim));
+  launch_attn<false>(s, a, B);
+}
+
+void rope_attention(cudaStream_t s, const void* qkv, const float* cos_t, const float* sin_t, const int* pos,
+                    void* k_cache, void* v_cache, void* out, int B, int Hq, int Hkv, int Lmax, int splits) {
+  check_attn(Hq, Hkv, splits);
+  AttnArgs a{};
+  a.q = static_cast<const __nv_bfloat16*>(qkv);
+  a.cos_t = cos_t;
+  a.sin_t = sin_t;
+  a.pos = pos;
+  a.k_cache = static_cast<__nv_bfloat16*>(k_cache);
+  a.v_cache = static_cast<__nv_bfloat16*>(v_cache);
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.q_stride = (Hq + 2 * Hkv) * kHeadDim;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.Lmax = Lmax;
+  a.splits = splits;
+  a.scale = 1.f / sqrtf(static_cast<float>(kHeadDim));
+  launch_attn<true>(s, a, B);
 }
 
 int attention_splits(int B, int Hkv, int context, int sms) {
-  // about two CTAs per SM, at least 16 positions per split
+  // about two CTAs per SM, at least 32 positions per split, one cluster of
+  // a power-of-two size (those pack the GPCs without holes)
   const int want = std::max(1, (2 * sms) / std::max(1, B * Hkv));
-  const int most = std::max(1, (context + 15) / 16);
-  return std::max(1, std::min({want, most, 128}));
+  const int most = std::max(1, (context + 31) / 32);
+  const int cap = std::min({want, most, kMaxAttnSplits});
+  int sp = 1;
+  while (sp * 2 <= cap) sp *= 2;
+  return sp;
 }
 
 void silu_mul(cudaStream_t s, const void* gu, void* out, int B, int I) {

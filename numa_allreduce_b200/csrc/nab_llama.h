@@ -10,12 +10,16 @@ namespace nab {
 void rope_append(cudaStream_t s, const void* qkv, const float* cos_t, const float* sin_t, const int* pos,
                  void* q_out, void* k_cache, void* v_cache, int B, int Hq, int Hkv, int Lmax);
 
-// GQA decode attention over positions [0, *pos]; part_ml holds B*Hq*splits*2
-// floats and part_o B*Hq*splits*128 floats of scratch; counters B*Hkv ints
-// that start at zero (the kernel leaves them at zero).
+// GQA decode attention over positions [0, *pos] of the cache, q [B, Hq, 128]
+// (already rotated). splits in [1, 16] CTAs per (batch, kv head), combined
+// in the same launch; no scratch.
 void decode_attention(cudaStream_t s, const void* q, const void* k_cache, const void* v_cache, const int* pos,
-                      float* part_ml, float* part_o, int* counters, void* out, int B, int Hq, int Hkv, int Lmax,
-                      int splits);
+                      void* out, int B, int Hq, int Hkv, int Lmax, int splits);
+// RoPE + KV append + attention in one launch, from the qkv projection
+// [B, (Hq + 2 Hkv) * 128]: the same result as rope_append then
+// decode_attention.
+void rope_attention(cudaStream_t s, const void* qkv, const float* cos_t, const float* sin_t, const int* pos,
+                    void* k_cache, void* v_cache, void* out, int B, int Hq, int Hkv, int Lmax, int splits);
 // Sequence splits that give about two CTAs per SM.
 int attention_splits(int B, int Hkv, int context, int sms);
 

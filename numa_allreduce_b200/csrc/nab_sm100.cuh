@@ -62,6 +62,14 @@ NAB_DINLINE void tma_load_2d(void* smem_dst, const CUtensorMap* map, int32_t x, 
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
 }
+// 1-D bulk copy global -> this CTA's shared memory (no multicast); both
+// addresses 16-byte aligned, bytes a multiple of 16.
+NAB_DINLINE void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(smem_dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
 NAB_DINLINE void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -145,6 +153,11 @@ NAB_DINLINE uint32_t dsmem_addr(uint32_t local_smem_addr, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_smem_addr), "r"(rank));
   return r;
+}
+NAB_DINLINE float ld_dsmem_f32(uint32_t cluster_addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
+  return v;
 }
 NAB_DINLINE float4 ld_dsmem_f4(uint32_t cluster_addr) {
   float4 v;

@@ -358,18 +358,26 @@ void rope_append_op(const at::Tensor& qkv, const at::Tensor& cos_t, const at::Te
 }
 
 void decode_attention_op(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
-                         const at::Tensor& pos, at::Tensor& part_ml, at::Tensor& part_o, at::Tensor& counters,
-                         at::Tensor& out, int64_t splits) {
-  TORCH_CHECK(q.dim() == 3 && q.size(2) == 128 && k_cache.dim() == 4, "decode_attention: shapes");
+                         const at::Tensor& pos, at::Tensor& out, int64_t splits) {
+  TORCH_CHECK(q.dim() == 3 && q.size(2) == 128 && k_cache.dim() == 4 && q.is_contiguous(), "decode_attention: shapes");
   const int64_t B = q.size(0), Hq = q.size(1), Hkv = k_cache.size(1);
-  TORCH_CHECK(part_ml.numel() >= B * Hq * splits * 2 && part_o.numel() >= B * Hq * splits * 128,
-              "decode_attention: scratch too small");
-  TORCH_CHECK(counters.scalar_type() == at::kInt && counters.numel() >= B * Hkv, "decode_attention: counters");
   const at::cuda::OptionalCUDAGuard guard(q.device());
   nab::decode_attention(at::cuda::getCurrentCUDAStream().stream(), q.data_ptr(), k_cache.data_ptr(),
-                        v_cache.data_ptr(), pos.data_ptr<int>(), part_ml.data_ptr<float>(), part_o.data_ptr<float>(),
-                        counters.data_ptr<int>(), out.data_ptr(), static_cast<int>(B), static_cast<int>(Hq),
-                        static_cast<int>(Hkv), static_cast<int>(k_cache.size(2)), static_cast<int>(splits));
+                        v_cache.data_ptr(), pos.data_ptr<int>(), out.data_ptr(), static_cast<int>(B),
+                        static_cast<int>(Hq), static_cast<int>(Hkv), static_cast<int>(k_cache.size(2)),
+                        static_cast<int>(splits));
+}
+
+void rope_attention_op(const at::Tensor& qkv, const at::Tensor& cos, const at::Tensor& sin, const at::Tensor& pos,
+                       at::Tensor& k_cache, at::Tensor& v_cache, at::Tensor& out, int64_t Hq, int64_t Hkv,
+                       int64_t splits) {
+  TORCH_CHECK(qkv.dim() == 2 && qkv.size(1) == (Hq + 2 * Hkv) * 128 && qkv.is_contiguous(), "rope_attention: qkv");
+  TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(1) == Hkv && cos.scalar_type() == at::kFloat, "rope_attention: shapes");
+  const at::cuda::OptionalCUDAGuard guard(qkv.device());
+  nab::rope_attention(at::cuda::getCurrentCUDAStream().stream(), qkv.data_ptr(), cos.data_ptr<float>(),
+                      sin.data_ptr<float>(), pos.data_ptr<int>(), k_cache.data_ptr(), v_cache.data_ptr(),
+                      out.data_ptr(), static_cast<int>(qkv.size(0)), static_cast<int>(Hq), static_cast<int>(Hkv),
+                      static_cast<int>(k_cache.size(2)), static_cast<int>(splits));
 }
 
 int64_t attention_splits(int64_t B, int64_t Hkv, int64_t context) {
@@ -447,8 +455,10 @@ TORCH_LIBRARY(nab, m) {
   m.def("rope_append(Tensor qkv, Tensor cos, Tensor sin, Tensor pos, Tensor(a!) q_out, Tensor(b!) k_cache, "
         "Tensor(c!) v_cache, int Hq, int Hkv) -> ()");
   m.impl("rope_append", c10::kCUDA, &rope_append_op);
-  m.def("decode_attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor pos, Tensor(a!) part_ml, "
-        "Tensor(b!) part_o, Tensor(d!) counters, Tensor(c!) out, int splits) -> ()");
+  m.def("decode_attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor pos, Tensor(a!) out, int splits) -> ()");
+  m.def("rope_attention(Tensor qkv, Tensor cos, Tensor sin, Tensor pos, Tensor(a!) k_cache, Tensor(b!) v_cache, "
+        "Tensor(c!) out, int Hq, int Hkv, int splits) -> ()");
+  m.impl("rope_attention", c10::kCUDA, &rope_attention_op);
   m.def("attention_splits(int B, int Hkv, int context) -> int", &attention_splits);
   m.impl("decode_attention", c10::kCUDA, &decode_attention_op);
   m.def("silu_mul(Tensor gu, Tensor(a!) out) -> ()");

@@ -1,4 +1,4 @@
-"""Tensor-parallel Llama decoder for CUDA-graph decode (BASELINE config 5).
+"""Tensor-parallel Llama decoder for CUDA-graph decode.
 
 Llama-3 architecture (GQA attention with rotary embeddings, SwiGLU MLP,
 RMSNorm), sharded Megatron-style over the ranks: q/k/v and gate/up
@@ -17,9 +17,9 @@ next RMSNorm:
 * ``impl="baseline"``: cuBLAS (``F.linear``) + NCCL ``all_reduce`` + residual
   add + ``F.rms_norm``, the unfused stack.
 
-Attention (decode over a synthetic KV cache), RoPE and SwiGLU use this
-library's kernels in both variants so the comparison isolates the
-projections and the allreduces. Weights are random N(0, 0.02) (there is no
+Attention (decode over a synthetic KV cache) uses this library's kernels in
+both variants: the baseline as separate RoPE/KV-append and attention
+launches, the fused variant as one launch that does both. Weights are random N(0, 0.02) (there is no
 checkpoint), the KV cache random N(0, 1); every buffer a step touches is
 static so the whole step is captured in one CUDA graph.
 """
@@ -149,9 +149,6 @@ class LlamaTPDecoder:
         self.y = torch.empty(batch, H, **bf)
         self.logits = torch.empty(batch, self.v_local, **bf)
         self.splits = attn_splits or int(self.ops.attention_splits(batch, self.Hkv, context + 1))
-        self.attn_counters = torch.zeros(batch * self.Hkv, device=self.device, dtype=torch.int32)
-        self.part_ml = torch.empty(batch * self.Hq * self.splits * 2, device=self.device, dtype=torch.float32)
-        self.part_o = torch.empty(batch * self.Hq * self.splits * D, device=self.device, dtype=torch.float32)
         self.gemm_splits = {}
         self.next_tokens = torch.zeros(batch, device=self.device, dtype=torch.long)
         self._gathered = torch.empty(W * batch * 2, device=self.device, dtype=torch.float32)
@@ -201,9 +198,13 @@ class LlamaTPDecoder:
         self.x.copy_(F.rms_norm(self.h, (cfg.hidden,), self.layers[0]["in_norm"], cfg.eps))
         for i, L in enumerate(self.layers):
             self._proj(self.x, self._w(i, "wqkv"), self.qkv)
-            ops.rope_append(self.qkv, self.cos, self.sin, self.pos, self.q, L["k"], L["v"], self.Hq, self.Hkv)
-            ops.decode_attention(self.q, L["k"], L["v"], self.pos, self.part_ml, self.part_o, self.attn_counters,
-                                 self.attn.view(self.B, self.Hq, cfg.head_dim), self.splits)
+            attn = self.attn.view(self.B, self.Hq, cfg.head_dim)
+            if self.impl == "baseline":
+                ops.rope_append(self.qkv, self.cos, self.sin, self.pos, self.q, L["k"], L["v"], self.Hq, self.Hkv)
+                ops.decode_attention(self.q, L["k"], L["v"], self.pos, attn, self.splits)
+            else:
+                ops.rope_attention(self.qkv, self.cos, self.sin, self.pos, L["k"], L["v"], attn, self.Hq, self.Hkv,
+                                   self.splits)
             self._row_parallel_tail(self.attn, self._w(i, "wo"), L["post_norm"])
             if self.impl == "baseline":
                 self._proj(self.x, self._w(i, "wgu"), self.gu)

@@ -71,7 +71,7 @@ def test_hierarchical_bit_exact(groups, dtype):
 
 
 def test_hier_matches_numa_config_tolerance():
-    """BASELINE config 3 shape (2 groups of 4, bf16 1 MB) against an fp32 sum."""
+    """Hierarchical shape (2 groups of 4, bf16 1 MB) against an fp32 sum."""
     groups = [[0, 1, 2, 3], [4, 5, 6, 7]]
     with EmulatedGroup(8, groups=groups) as g:
         xs = _inputs(8, (1 << 20) // 2, torch.bfloat16, seed=7)

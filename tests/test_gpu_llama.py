@@ -13,11 +13,10 @@ from numa_allreduce_b200.ops import _ext
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("B,Hq,Hkv,L,splits", [(1, 8, 1, 1025, 64), (4, 16, 8, 300, 5), (2, 8, 2, 64, 1),
-                                              (1, 8, 1, 3, 16), (3, 8, 1, 1025, 0)])
+@pytest.mark.parametrize("B,Hq,Hkv,L,splits", [(1, 8, 1, 1025, 16), (4, 16, 8, 300, 5), (2, 8, 2, 64, 1),
+                                              (1, 8, 1, 3, 16), (3, 8, 1, 1025, 0), (2, 4, 4, 77, 3)])
 def test_decode_attention(B, Hq, Hkv, L, splits):
-    """One launch: split partials and the combine by the last CTA; repeated
-    calls check that the arrival counters reset themselves."""
+    """Split partials combined over the cluster's shared memory, one launch."""
     ops = _ext.load()
     Lmax = ((L + 63) // 64) * 64
     g = torch.Generator(device="cuda").manual_seed(0)
@@ -26,15 +25,38 @@ def test_decode_attention(B, Hq, Hkv, L, splits):
     v = torch.randn(B, Hkv, Lmax, 128, generator=g, device="cuda").to(torch.bfloat16)
     pos = torch.tensor([L - 1], device="cuda", dtype=torch.int32)
     splits = splits or int(ops.attention_splits(B, Hkv, L))
-    ml = torch.empty(B * Hq * splits * 2, device="cuda")
-    po = torch.empty(B * Hq * splits * 128, device="cuda")
-    counters = torch.zeros(B * Hkv, device="cuda", dtype=torch.int32)
     ref = reference_attention(q, k, v, L)
-    for _ in range(3):
+    for _ in range(2):
         out = torch.zeros(B, Hq, 128, device="cuda", dtype=torch.bfloat16)
-        ops.decode_attention(q, k, v, pos, ml, po, counters, out, splits)
+        ops.decode_attention(q, k, v, pos, out, splits)
         torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
-    assert int(counters.abs().sum()) == 0
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,pos,splits", [(1, 8, 1, 1024, 16), (3, 8, 2, 40, 4), (2, 8, 1, 0, 1)])
+def test_rope_attention_matches_two_launches(B, Hq, Hkv, pos, splits):
+    """RoPE + KV append + attention in one launch == rope_append, then decode_attention."""
+    ops = _ext.load()
+    D, Lmax = 128, ((pos + 1 + 63) // 64) * 64
+    g = torch.Generator(device="cuda").manual_seed(3)
+    qkv = torch.randn(B, (Hq + 2 * Hkv) * D, generator=g, device="cuda").to(torch.bfloat16)
+    k0 = torch.randn(B, Hkv, Lmax, D, generator=g, device="cuda").to(torch.bfloat16)
+    v0 = torch.randn(B, Hkv, Lmax, D, generator=g, device="cuda").to(torch.bfloat16)
+    inv = 1.0 / (500000.0 ** (torch.arange(0, D, 2, device="cuda", dtype=torch.float64) / D))
+    ang = torch.arange(Lmax, device="cuda", dtype=torch.float64)[:, None] * inv[None, :]
+    cos, sin = ang.cos().float().contiguous(), ang.sin().float().contiguous()
+    p = torch.tensor([pos], device="cuda", dtype=torch.int32)
+    k1, v1 = k0.clone(), v0.clone()
+    q = torch.empty(B, Hq, D, device="cuda", dtype=torch.bfloat16)
+    ops.rope_append(qkv, cos, sin, p, q, k1, v1, Hq, Hkv)
+    ref = torch.empty(B, Hq, D, device="cuda", dtype=torch.bfloat16)
+    ops.decode_attention(q, k1, v1, p, ref, splits)
+    k2, v2 = k0.clone(), v0.clone()
+    out = torch.empty(B, Hq, D, device="cuda", dtype=torch.bfloat16)
+    ops.rope_attention(qkv, cos, sin, p, k2, v2, out, Hq, Hkv, splits)
+    torch.cuda.synchronize()
+    assert torch.equal(k1, k2) and torch.equal(v1, v2)
+    torch.testing.assert_close(out.float(), ref.float(), rtol=1e-2, atol=1e-2)
+    torch.testing.assert_close(out.float(), reference_attention(q, k1, v1, pos + 1), rtol=2e-2, atol=2e-2)
 
 
 def test_rope_append():

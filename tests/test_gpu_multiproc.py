@@ -139,8 +139,8 @@ def _worker_graph(rank, ws, port, algo):
 
 
 def _worker_gemm_ar(rank, ws, port):
-    """Fused row-parallel GEMM + allreduce + residual + RMSNorm (BASELINE
-    config 4 shapes) against a PyTorch fp32 reference of the same layer."""
+    """Fused row-parallel GEMM + allreduce + residual + RMSNorm (Llama-3-8B
+    down_proj shapes) against a PyTorch fp32 reference of the same layer."""
     from numa_allreduce_b200 import NumaAwareAllReduce
     from numa_allreduce_b200.ops.gemm import gemm_allreduce_rmsnorm, pack_weight
 

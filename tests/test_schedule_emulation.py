@@ -1,4 +1,5 @@
-"""Schedules and their gloo/CPU executor.
+"""Schedules and their gloo/CPU executor (the 3-stage hierarchical emulation on
+gloo ranks, fp32 [1024, 1024]).
 
 Config 1: world size 4 over gloo, the three-stage schedule with NUMA groups
 {0,1},{2,3}; each rank holds fp32 [1024, 1024] drawn from N(0,1) with
