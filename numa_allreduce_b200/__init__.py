@@ -11,12 +11,21 @@ Public API (parity with the reference's ``src/__init__.py``, which exported
 * :class:`HierSchedule` and :func:`emulate_allreduce`: the schedule and its
   gloo/CPU executor;
 * :func:`fused_allreduce_rmsnorm`, :func:`rmsnorm_residual`: the fused TP
-  layer tail.
+  layer tail;
+* :func:`gemm`, :func:`gemm_swiglu`, :func:`gemm_allreduce_rmsnorm`,
+  :func:`pack_weight`, :func:`interleave_gate_up`: the tcgen05 GEMM and its
+  fusions (SwiGLU epilogue; row-parallel GEMM -> allreduce -> residual ->
+  RMSNorm);
+* :class:`LlamaConfig`, :class:`LlamaTPDecoder`: the tensor-parallel decoder
+  built on them (in ``numa_allreduce_b200.models``, imported lazily);
+* :class:`PeerMonitor`, :class:`PeerLost`: host-side failure detection.
 """
 
 from .ops.fused import fused_allreduce_rmsnorm, rmsnorm_residual
+from .ops.gemm import PackedWeight, gemm, gemm_allreduce_rmsnorm, gemm_swiglu, interleave_gate_up, pack_weight
 from .parallel.comm import AllReduceError, NumaAwareAllReduce
 from .parallel.emulate import emulate_allreduce
+from .parallel.health import PeerLost, PeerMonitor
 from .parallel.schedule import HierSchedule, reference_allreduce
 from .parallel.select import AlgoSelector
 from .utils.topology import GpuNumaInfo, NumaNodeInfo, NumaTopology, detect_numa_topology
@@ -29,9 +38,17 @@ __all__ = [
     "NumaAwareAllReduce",
     "NumaNodeInfo",
     "NumaTopology",
+    "PackedWeight",
+    "PeerLost",
+    "PeerMonitor",
     "detect_numa_topology",
     "emulate_allreduce",
     "fused_allreduce_rmsnorm",
+    "gemm",
+    "gemm_allreduce_rmsnorm",
+    "gemm_swiglu",
+    "interleave_gate_up",
+    "pack_weight",
     "reference_allreduce",
     "rmsnorm_residual",
 ]
