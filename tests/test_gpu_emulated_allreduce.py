@@ -85,12 +85,12 @@ def test_back_to_back_calls_and_protocol_switches():
     ws = 4
     with EmulatedGroup(ws, chunk_max=16 << 10, groups=[[0, 1], [2, 3]]) as g:
         algos = ["oneshot", "twoshot", "hier", "twoshot_pipe"]
-        for i in range(300):
+        for i in range(1200):
             n = [8, 1000 * 8, 50000 * 8, 8 * 3][i % 4]
             algo = algos[i % 4]
             xs = _inputs(ws, n, torch.bfloat16, seed=i)
             outs = g.all_reduce(xs, algo=algo)
-            if i % 25 == 0 or i > 290:
+            if i % 50 == 0 or i > 1190:
                 sched = {"oneshot": HierSchedule.oneshot(ws), "twoshot": HierSchedule.twoshot(ws),
                          "twoshot_pipe": HierSchedule.twoshot(ws),
                          "hier": HierSchedule.from_groups([[0, 1], [2, 3]])}[algo]
