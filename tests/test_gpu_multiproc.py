@@ -194,6 +194,55 @@ def _worker_gemm_ar(rank, ws, port):
     assert not errors, errors[:5]
 
 
+def _worker_llama(rank, ws, port):
+    """Tensor-parallel decoder across processes: the fused path (tcgen05 GEMMs,
+    GEMM + allreduce + norm, and above 128 tokens cuBLAS + fused allreduce
+    norm) against the cuBLAS + NCCL baseline of the same step, and a CUDA-graph
+    replay of the fused step."""
+    from numa_allreduce_b200 import NumaAwareAllReduce
+    from numa_allreduce_b200.models.llama_tp import LlamaConfig, LlamaTPDecoder
+
+    _init(rank, ws, port)
+    errors = []
+    ar = None
+    try:
+        ar = NumaAwareAllReduce(dist.group.WORLD, device=rank)
+        for B in (2, 160):
+            m = LlamaTPDecoder(LlamaConfig.tiny(), ar, batch=B, context=50)
+            m.tokens.copy_(torch.arange(B, device="cuda") % 4000 + 1)
+            m.impl = "baseline"
+            m.step()
+            base = m.x.float().clone()
+            m.reset_position()
+            m.impl = "fused"
+            m.step()
+            torch.cuda.synchronize()
+            rel = ((m.x.float() - base).norm() / base.norm()).item()
+            if not rel < 3e-2:
+                errors.append(f"B={B}: fused vs baseline relative difference {rel}")
+            if B == 2:
+                eager = m.x.float().clone()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    m.step()
+                m.reset_position()
+                g.replay()
+                torch.cuda.synchronize()
+                if not torch.allclose(m.x.float(), eager, rtol=1e-3, atol=1e-3):
+                    errors.append("graph replay differs from the eager fused step")
+                del g
+        try:
+            ar.check()
+        except Exception as e:
+            errors.append(str(e))
+    finally:
+        torch.cuda.synchronize()
+        if ar is not None:
+            ar.close()
+        dist.destroy_process_group()
+    assert not errors, errors[:5]
+
+
 def _need(ws):
     if torch.cuda.device_count() < ws:
         pytest.skip(f"needs {ws} GPUs")
@@ -209,6 +258,11 @@ def test_correctness_multiprocess(ws):
 def test_gemm_allreduce_rmsnorm(ws):
     _need(ws)
     mp.spawn(_worker_gemm_ar, args=(ws, free_port()), nprocs=ws, join=True)
+
+
+def test_llama_tp_decoder_two_ranks():
+    _need(2)
+    mp.spawn(_worker_llama, args=(2, free_port()), nprocs=2, join=True)
 
 
 @pytest.mark.parametrize("algo", ["auto", "pull"])
