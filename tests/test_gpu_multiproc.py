@@ -243,6 +243,35 @@ def _worker_llama(rank, ws, port):
     assert not errors, errors[:5]
 
 
+def _worker_reinit(rank, ws, port):
+    """Repeated construction and close() in one process: every instance works
+    and device memory returns to where it started (no leaked IPC buffers)."""
+    from numa_allreduce_b200 import NumaAwareAllReduce
+
+    _init(rank, ws, port)
+    errors = []
+    try:
+        x = torch.full((1 << 16,), float(rank + 1), device="cuda", dtype=torch.bfloat16)
+        torch.cuda.synchronize()
+        free0 = torch.cuda.mem_get_info()[0]
+        for i in range(5):
+            ar = NumaAwareAllReduce(dist.group.WORLD, device=rank)
+            out = ar.custom_all_reduce(x)
+            torch.cuda.synchronize()
+            if out is None or not torch.all(out == sum(range(1, ws + 1))):
+                errors.append(f"instance {i}: wrong result")
+            ar.close()
+            del out
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        free1 = torch.cuda.mem_get_info()[0]
+        if free0 - free1 > (64 << 20):  # allow allocator slack, not 5 workspaces
+            errors.append(f"device memory not returned: {(free0 - free1) >> 20} MiB")
+    finally:
+        dist.destroy_process_group()
+    assert not errors, errors
+
+
 def _need(ws):
     if torch.cuda.device_count() < ws:
         pytest.skip(f"needs {ws} GPUs")
@@ -258,6 +287,11 @@ def test_correctness_multiprocess(ws):
 def test_gemm_allreduce_rmsnorm(ws):
     _need(ws)
     mp.spawn(_worker_gemm_ar, args=(ws, free_port()), nprocs=ws, join=True)
+
+
+def test_repeated_init_close_two_ranks():
+    _need(2)
+    mp.spawn(_worker_reinit, args=(2, free_port()), nprocs=2, join=True)
 
 
 def test_llama_tp_decoder_two_ranks():
