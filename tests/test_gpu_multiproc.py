@@ -272,6 +272,55 @@ def _worker_reinit(rank, ws, port):
     assert not errors, errors
 
 
+def _worker_perf(rank, ws, port, result_q):
+    """The reference's performance acceptance (tests/test_numa_all_reduce.py:
+    265-308): fp16 at 64 and 256 MiB, the custom path at least 0.8x NCCL's
+    speed. Device time: CUDA events per call, median, max over ranks."""
+    from numa_allreduce_b200 import NumaAwareAllReduce
+
+    _init(rank, ws, port)
+    ar = None
+    try:
+        ar = NumaAwareAllReduce(dist.group.WORLD, device=rank)
+
+        def timed(fn, iters=20, warmup=5):
+            for _ in range(warmup):
+                fn()
+            torch.cuda.synchronize()
+            dist.barrier()
+            evs = []
+            for _ in range(iters):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                fn()
+                b.record()
+                evs.append((a, b))
+            torch.cuda.synchronize()
+            med = sorted(a.elapsed_time(b) for a, b in evs)[iters // 2]
+            t = torch.tensor([med], device="cuda", dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return t.item()
+
+        res = {}
+        for mib in (64, 256):
+            n = (mib << 20) // 2
+            x = torch.randn(n, device="cuda").to(torch.float16)
+            out = torch.empty_like(x)
+            y = x.clone()
+            t_ours = timed(lambda: ar.all_reduce(x, out))
+            t_nccl = timed(lambda: dist.all_reduce(y))
+            res[mib] = (t_ours, t_nccl)
+            del x, out, y
+        ar.check()
+        if rank == 0:
+            result_q.put(res)
+    finally:
+        torch.cuda.synchronize()
+        if ar is not None:
+            ar.close()
+        dist.destroy_process_group()
+
+
 def _need(ws):
     if torch.cuda.device_count() < ws:
         pytest.skip(f"needs {ws} GPUs")
@@ -287,6 +336,15 @@ def test_correctness_multiprocess(ws):
 def test_gemm_allreduce_rmsnorm(ws):
     _need(ws)
     mp.spawn(_worker_gemm_ar, args=(ws, free_port()), nprocs=ws, join=True)
+
+
+def test_performance_vs_nccl_fp16_ws4():
+    _need(4)
+    q = mp.get_context("spawn").Queue()
+    mp.spawn(_worker_perf, args=(4, free_port(), q), nprocs=4, join=True)
+    res = q.get(timeout=30)
+    for mib, (ours, nccl) in res.items():
+        assert nccl / ours >= 0.8, f"{mib} MiB: custom {ours:.3f} ms vs NCCL {nccl:.3f} ms"
 
 
 def test_repeated_init_close_two_ranks():
