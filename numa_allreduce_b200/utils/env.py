@@ -21,6 +21,9 @@ reads. Every variable below is actually read:
 ``NAB_NVTX``               ``1`` wraps calls in NVTX ranges
 ``NAB_PIPE_CTAS``          CTAs of the pipelined two-shot (default 128)
 ``NAB_PIPE_TILE``          bytes per ring slot of the pipelined two-shot
+``NAB_GEMM_PDL``           ``0`` launches the GEMMs without programmatic
+                           dependent launch (read by the native code)
+``NAB_NO_BUILD``           ``1``: never compile the extension on import
 =========================  ===================================================
 """
 
