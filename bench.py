@@ -26,6 +26,7 @@ import os
 import socket
 import statistics
 import sys
+import time
 import traceback
 from datetime import timedelta
 
@@ -50,6 +51,7 @@ def parse_args():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--sizes", type=str, default=None, help="comma-separated bytes per rank")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-graph", action="store_true", help="skip the per-size CUDA-graph replay timing")
     return p.parse_args()
 
 
@@ -89,6 +91,13 @@ class OursArm:
     def launches(self) -> int:
         return self.ar.launches
 
+    def capture(self, x, out, s, calls):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(calls):
+                self.step_one(x, out, s)
+        return g
+
     def close(self):
         self.ar.close()
 
@@ -118,6 +127,22 @@ class ReferenceArm:
 
     def launches(self):
         return None
+
+    def capture(self, x, out, s, calls):
+        """The reference's own capture flow (src/numa_all_reduce.py:362-413):
+        a warm-up call inside ``capture()``, then the graph; leaving the
+        context registers the captured buffers on every rank."""
+        g = torch.cuda.CUDAGraph()
+        with self.ar.capture():
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                self.step_one(x, out, s)
+            torch.cuda.current_stream().wait_stream(side)
+            with torch.cuda.graph(g):
+                for _ in range(calls):
+                    self.step_one(x, out, s)
+        return g
 
     def close(self):
         if not self.ar.disabled:
@@ -152,6 +177,7 @@ def timed_sweep(arm, xs, outs, sizes, steps, warmup, rank, bus_ids):
     dist.barrier()
     torch.cuda.synchronize()
     l0 = arm.launches()
+    t_host0 = time.time()
     start.record()
     for k in range(steps):
         for s in sizes:
@@ -161,14 +187,50 @@ def timed_sweep(arm, xs, outs, sizes, steps, warmup, rank, bus_ids):
             b.record()
     end.record()
     torch.cuda.synchronize()
+    t_host1 = time.time()
     l1 = arm.launches()
     dist.barrier()
-    clocks = sampler.stop() if sampler else None
+    clocks = sampler.stop(t_host0, t_host1) if sampler else None
     total_ms = start.elapsed_time(end)
     p50 = [statistics.median(a.elapsed_time(b) * 1e3 for a, b in ev[s]) for s in sizes]
     maxed = _max_over_ranks([total_ms] + p50)
     launches = None if l0 is None else _sum_over_ranks(l1 - l0)
     return maxed[0], maxed[1:], clocks, launches
+
+
+def timed_graph(arm, xs, outs, sizes, calls=10, reps=5):
+    """Per-size device time per call with the calls replayed from a CUDA graph
+    (no host launch gap between them): ``calls`` calls captured once, the
+    graph replayed ``reps`` times, max over ranks. Every rank captures the
+    same sizes; a size whose capture failed on any rank reports None."""
+    res = []
+    for s in sizes:
+        g = None
+        ok = True
+        try:
+            g = arm.capture(xs[s], outs[s], s, calls)
+        except Exception as e:  # pragma: no cover - depends on the arm
+            ok = False
+            print(f"graph capture of {s} bytes failed on this rank: {e}", file=sys.stderr)
+        flag = torch.tensor([1 if ok else 0], device="cuda")
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        us = -1.0
+        if bool(flag.item()):
+            g.replay()
+            torch.cuda.synchronize()
+            dist.barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(reps):
+                g.replay()
+            b.record()
+            torch.cuda.synchronize()
+            us = a.elapsed_time(b) * 1e3 / (reps * calls)
+        del g  # graphs holding NCCL calls go before the process group does
+        torch.cuda.synchronize()
+        res.append(us)
+    maxed = _max_over_ranks(res)
+    return [None if v < 0 else v for v in maxed]
 
 
 def timed_e2e(arm, xs, outs, sizes, steps, warmup):
@@ -246,6 +308,7 @@ def main():
         total_ms, p50_us, clocks, launches = timed_sweep(arm, xs, outs, sizes, args.steps, args.warmup,
                                                          rank, bus)
         e2e_ms = None if args.no_e2e else timed_e2e(arm, xs, outs, sizes, args.steps, min(args.warmup, 2))
+        graph_us = None if args.no_graph else timed_graph(arm, xs, outs, sizes)
         bytes_per_step = sum(sizes)
         ms_per_step = total_ms / args.steps
         value = world * bytes_per_step / (ms_per_step / 1e3) / 1e9
@@ -254,6 +317,10 @@ def main():
                       "busbw_gbs": round(busbw_gbs(s, t / 1e6, world), 1),
                       "algbw_gbs": round(s / (t / 1e6) / 1e9, 1), "algo": arm.algos[s]}
                      for s, t in zip(sizes, p50_us)]
+            if graph_us is not None:
+                for row, t in zip(sweep, graph_us):
+                    row["graph_us"] = None if t is None else round(t, 2)
+                    row["graph_busbw_gbs"] = None if t is None else round(busbw_gbs(row["bytes"], t / 1e6, world), 1)
             line = {
                 "metric": METRIC,
                 "value": round(value, 2),
@@ -276,7 +343,9 @@ def main():
                     "value_definition": "n_gpus * bytes per rank per step / device time per step (aggregate algbw)",
                     "l2": "inputs larger than L2: a step touches 512 MiB per rank; each buffer is re-read only "
                           "after >256 MiB of other traffic",
-                    "timing": "CUDA events on the launching stream, max over ranks; per-size p50 over steps",
+                    "timing": "CUDA events on the launching stream, max over ranks; per-size p50 over steps; "
+                              "sweep[].graph_us: per call, 10 calls replayed from one CUDA graph (after the "
+                              "timed region, not part of value)",
                 },
                 "sweep": sweep,
                 "sweep_busbw_gbs": round(busbw_gbs(bytes_per_step, ms_per_step / 1e3, world), 1),

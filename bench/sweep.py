@@ -56,7 +56,33 @@ def parse():
     p.add_argument("--hier-groups", default=None, help="e.g. 0,1,2,3|4,5,6,7")
     p.add_argument("--pipe-configs", default=None,
                    help="extra pipelined two-shot configurations to time, e.g. 148x256,128x512 (CTAs x tile KiB)")
+    p.add_argument("--hybrid-configs", default=None,
+                   help="hybrid splits to time, e.g. 400x64x80,300x56x88 (P2P per mille x P2P CTAs x NVLS CTAs); "
+                        "--write-table keeps the one with the best bus bandwidth summed over sizes >= 16 MiB")
+    p.add_argument("--merge", action="store_true",
+                   help="--write-table replaces only this world size's entries of an existing table")
     return p.parse_args()
+
+
+def pick_hybrid(rows):
+    """Best hybrid split of a sweep: highest bus bandwidth summed over the
+    sizes of at least 16 MiB. Returns (split, rows relabelled "hybrid")."""
+    score = {}
+    for r in rows:
+        if r["algo"].startswith("hybrid:") and r["bytes"] >= (16 << 20):
+            score[r["algo"]] = score.get(r["algo"], 0.0) + r["busbw_gbs"]
+    if not score:
+        return None, [r for r in rows if not r["algo"].startswith("hybrid:")]
+    best = max(score, key=score.get)
+    split = tuple(int(v) for v in best.split(":")[1].split("x"))
+    out = []
+    for r in rows:
+        if r["algo"].startswith("hybrid:"):
+            if r["algo"] == best:
+                out.append(dict(r, algo="hybrid"))
+        elif r["algo"] != "hybrid":
+            out.append(r)
+    return split, out
 
 
 def max_over_ranks(vals):
@@ -142,7 +168,8 @@ def main():
                                              pipe_tile=tile_kib << 10)))
     sizes = [int(v) for v in args.sizes.split(",")]
     if args.algos == "all":
-        algos = ["oneshot", "twoshot", "twoshot_pipe"] + (["nvls_oneshot", "nvls_twoshot"] if ar.has_nvls else []) + \
+        algos = ["oneshot", "twoshot", "twoshot_pipe"] + (
+            ["nvls_oneshot", "nvls_twoshot"] + ([] if args.hybrid_configs else ["hybrid"]) if ar.has_nvls else []) + \
                 (["hier"] if ar.hier_groups else [])
     elif args.algos == "auto":
         algos = ["auto"]
@@ -170,6 +197,14 @@ def main():
                               (lambda nm=name: ar.all_reduce(x, out=out, algo=nm)), True))
             for label, comm in extra:
                 cands.append((label, (lambda c=comm: c.all_reduce(x, out=out, algo="twoshot_pipe")), True))
+            if args.hybrid_configs and ar.has_nvls:
+                for spec in args.hybrid_configs.split(","):
+                    split = tuple(int(v) for v in spec.split("x"))
+
+                    def run_hybrid(split=split):
+                        ar.set_hybrid(*split)
+                        return ar.all_reduce(x, out=out, algo="hybrid")
+                    cands.append((f"hybrid:{spec}", run_hybrid, True))
             if args.nccl:
                 y = x.clone()
                 cands.append(("nccl", lambda: dist.all_reduce(y), False))
@@ -187,6 +222,8 @@ def main():
                 dist.all_reduce(flag, op=dist.ReduceOp.MIN)
                 modes = ["eager"] if not ours or args.mode == "eager" else (
                     ["graph"] if args.mode == "graph" else ["eager", "graph"])
+                if not ours and args.mode == "graph":
+                    modes = []
                 for mode in modes:
                     if mode == "eager":
                         us = time_eager(fn, args.iters, args.warmup)
@@ -206,10 +243,22 @@ def main():
             with open(args.out, "w") as f:
                 json.dump({"world_size": world, "nvls": ar.has_nvls, "rows": rows}, f, indent=1)
         if args.write_table:
-            tab_rows = [dict(r, algo=r["algo"].split(":")[-1]) for r in rows
-                        if r["mode"] == "eager" and r["correct"] and not r["algo"].startswith("ref")]
+            tab_rows = [dict(r, algo=r["algo"].split(":")[-1] if r["algo"].startswith("auto:") else r["algo"])
+                        for r in rows
+                        if r["mode"] == "eager" and r["correct"] and not r["algo"].startswith(("ref", "pipe_"))]
+            split, tab_rows = pick_hybrid(tab_rows)
+            table = build_table(tab_rows, hybrid={world: split} if split else None)
+            if args.merge and os.path.exists(args.write_table):
+                with open(args.write_table) as f:
+                    old = json.load(f)
+                table["entries"] = [e for e in old.get("entries", []) if e["world_size"] != world] + table["entries"]
+                table["entries"].sort(key=lambda e: (e["world_size"], e["dtype"], e["nvls"]))
+                hyb = {k: v for k, v in old.get("hybrid", {}).items() if k != str(world)}
+                hyb.update(table.get("hybrid", {}))
+                if hyb:
+                    table["hybrid"] = hyb
             with open(args.write_table, "w") as f:
-                json.dump(build_table(tab_rows), f, indent=1)
+                json.dump(table, f, indent=1)
     torch.cuda.synchronize()
     ar.close()
     for _, comm in extra:

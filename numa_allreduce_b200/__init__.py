@@ -18,9 +18,12 @@ Public API (parity with the reference's ``src/__init__.py``, which exported
   RMSNorm);
 * :class:`LlamaConfig`, :class:`LlamaTPDecoder`: the tensor-parallel decoder
   built on them (in ``numa_allreduce_b200.models``, imported lazily);
-* :class:`PeerMonitor`, :class:`PeerLost`: host-side failure detection.
+* :class:`PeerMonitor`, :class:`PeerLost`: host-side failure detection;
+  :func:`check_kernels`, :class:`KernelError`: the error record of the GEMM
+  and attention kernels' bounded waits.
 """
 
+from .ops.errors import KernelError, check_kernels, reset_kernels
 from .ops.fused import fused_allreduce_rmsnorm, rmsnorm_residual
 from .ops.gemm import PackedWeight, gemm, gemm_allreduce_rmsnorm, gemm_swiglu, interleave_gate_up, pack_weight
 from .parallel.comm import AllReduceError, NumaAwareAllReduce
@@ -35,12 +38,14 @@ __all__ = [
     "AllReduceError",
     "GpuNumaInfo",
     "HierSchedule",
+    "KernelError",
     "NumaAwareAllReduce",
     "NumaNodeInfo",
     "NumaTopology",
     "PackedWeight",
     "PeerLost",
     "PeerMonitor",
+    "check_kernels",
     "detect_numa_topology",
     "emulate_allreduce",
     "fused_allreduce_rmsnorm",
@@ -50,6 +55,7 @@ __all__ = [
     "interleave_gate_up",
     "pack_weight",
     "reference_allreduce",
+    "reset_kernels",
     "rmsnorm_residual",
 ]
 

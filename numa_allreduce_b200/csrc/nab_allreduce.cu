@@ -55,6 +55,35 @@ NAB_DINLINE bool exchange(const RankView& me, int kind, int slot, uint64_t seq, 
   return ::nab::exchange(me.wsp, me.rank, kind, slot, seq, peers, npeers, w, stage);
 }
 
+// Debug builds: checks of a launch made by every CTA before it touches any
+// memory (the rank, the world size, the flag slot of this CTA, 16-byte
+// aligned buffers and, through region_ok, that this CTA's slots lie inside
+// the workspace). A CTA whose check fails records it and returns; its peers'
+// bounded waits then run out. Always true in release builds.
+NAB_DINLINE bool launch_ok(const ARParams& p, const RankView& me, int ws, bool region_ok) {
+  if (!NAB_DEBUG_BOUNDS) return true;
+  const bool ok = me.rank >= 0 && me.rank < ws && p.ws == ws && blockIdx.x < kMaxBlocks && p.npacks > 0 &&
+                  ((reinterpret_cast<uintptr_t>(me.in) | reinterpret_cast<uintptr_t>(me.out)) & 15u) == 0 &&
+                  region_ok;
+  return dbg_ok(ok, p.err, p.err_host, static_cast<uint32_t>(me.rank));
+}
+
+// Debug builds: a pack index below its bound (records and skips the access
+// otherwise).
+#define NAB_DBG_IDX(idx, n) (!NAB_DEBUG_BOUNDS || dbg_ok((idx) < (n), p.err, p.err_host, static_cast<uint32_t>(idx)))
+
+// Slot regions of CTA c inside the IPC / multicast workspaces (debug checks).
+template <int WS>
+NAB_DINLINE bool pipe_region_ok(const ARParams& p, int c, int chp) {
+  return c < p.L.pipe_ctas && static_cast<int64_t>(chp) * 16 <= p.L.pipe_chunk &&
+         p.L.pipe_off + static_cast<int64_t>(c + 1) * kPipeSlots * 2 * WS * p.L.pipe_chunk <= p.L.ws_bytes;
+}
+template <int WS>
+NAB_DINLINE bool nvls_region_ok(const ARParams& p, const RankView& me, int c, int chp) {
+  return me.mc != nullptr && me.uc != nullptr && c < kNvlsCtas && static_cast<int64_t>(chp) * 16 <= p.L.nvls_chunk &&
+         p.L.mc_twoshot_off + static_cast<int64_t>(c + 1) * kNvlsSlots * WS * p.L.nvls_chunk <= p.L.mc_bytes;
+}
+
 // ------------------------------------------------------------------ copy ----
 __global__ void __launch_bounds__(kThreads) k_copy(const __grid_constant__ ARParams p) {
   const RankView& me = p.v[blockIdx.y];
@@ -92,6 +121,9 @@ __global__ void __launch_bounds__(kThreads, 2) k_oneshot(const __grid_constant__
   constexpr int U = 4;
   constexpr int UR = Unroll<WS>::kRed;
   const RankView& me = p.v[blockIdx.y];
+  if (!launch_ok(p, me, WS, p.npacks * 16 <= p.L.oneshot_max &&
+                                p.L.oneshot_off + 2 * WS * p.L.oneshot_max <= p.L.ws_bytes))
+    return;
   const int rank = me.rank;
   const uint32_t epoch = begin_call(me);
   const WaitCtx w = make_wait(p, me, epoch);
@@ -116,7 +148,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_oneshot(const __grid_constant__
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int64_t i = i0 + static_cast<int64_t>(u) * blockDim.x;
-      if (i < end) {
+      if (i < end && NAB_DBG_IDX(i, slot_packs)) {
 #pragma unroll
         for (int k = 1; k < WS; ++k) st_plain(slot((rank + k) % WS, rank) + i, x[u]);
       }
@@ -161,6 +193,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_twoshot(const __grid_constant__
   constexpr int UP = Unroll<WS>::kPeer;
   constexpr int UR = Unroll<WS>::kRed;
   const RankView& me = p.v[blockIdx.y];
+  if (!launch_ok(p, me, WS, static_cast<int>(blockIdx.x) < p.L.max_ctas &&
+                                static_cast<int64_t>(p.chunk_packs) * 16 <= p.L.chunk_max &&
+                                p.L.twoshot_off + static_cast<int64_t>(blockIdx.x + 1) * (WS + 1) * p.L.chunk_max <=
+                                    p.L.ws_bytes))
+    return;
   const int rank = me.rank;
   const uint32_t epoch = begin_call(me);
   const WaitCtx w = make_wait(p, me, epoch);
@@ -312,28 +349,24 @@ NAB_DINLINE bool wait_geq_cta(const uint64_t* addr, uint64_t target, const WaitC
   }
 }
 
+// Body of the pipelined P2P two-shot for CTA c of C on packs [0, npacks) of
+// src/dst (a hybrid launch passes a prefix of the message).
 template <typename T, int WS>
-__global__ void __launch_bounds__(kThreads, 1) k_twoshot_pipe(const __grid_constant__ ARParams p) {
+__device__ __forceinline__ void twoshot_pipe_body(const ARParams& p, const RankView& me, uint32_t epoch,
+                                                  const WaitCtx& w, int c, int C, const uint4* src, uint4* dst,
+                                                  int64_t npacks, int chp) {
   constexpr int S = kPipeSlots;
   constexpr int UP = Unroll<WS>::kPeer;
   constexpr int UR = Unroll<WS>::kRed;
-  const RankView& me = p.v[blockIdx.y];
   const int rank = me.rank;
-  const uint32_t epoch = begin_call(me);
-  const WaitCtx w = make_wait(p, me, epoch);
-  const int c = blockIdx.x;
-  const int C = gridDim.x;
-  const int chp = p.chunk_packs;
   const int64_t tile = static_cast<int64_t>(WS) * chp;
-  const int64_t ntiles = (p.npacks + tile - 1) / tile;
+  const int64_t ntiles = (npacks + tile - 1) / tile;
   const int64_t my_tiles = ntiles > c ? (ntiles - c + C - 1) / C : 0;
   const int64_t cstride = p.L.pipe_chunk / 16;
   const int64_t slot_packs = 2 * WS * cstride;  // [WS rs chunks][WS ag chunks]
   auto ring = [&](int r) -> uint4* {
     return reinterpret_cast<uint4*>(me.wsp[r] + p.L.pipe_off) + static_cast<int64_t>(c) * S * slot_packs;
   };
-  const uint4* src = reinterpret_cast<const uint4*>(me.in);
-  uint4* dst = reinterpret_cast<uint4*>(me.out);
   SignalPad* mypad = pad_of(me, rank);
   int peers[WS - 1];
   all_peers<WS>(rank, peers);
@@ -349,7 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_twoshot_pipe(const __grid_const
   volatile int64_t* done = &s_done;
   const int warp = threadIdx.x >> 5;
   auto chunk_len = [&](int64_t tb, int owner) -> int {
-    return static_cast<int>(span_len(chp, p.npacks - (tb + static_cast<int64_t>(owner) * chp)));
+    return static_cast<int>(span_len(chp, npacks - (tb + static_cast<int64_t>(owner) * chp)));
   };
 
   if (warp < kPushWarps) {
@@ -386,7 +419,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_twoshot_pipe(const __grid_const
           const int i = i0 + u * nt;
 #pragma unroll
           for (int q = 0; q < WS - 1; ++q)
-            if (i < len[q]) st_plain(ring(peers[q]) + slot * slot_packs + rank * cstride + i, x[u][q]);
+            if (i < len[q] && NAB_DBG_IDX(tb + static_cast<int64_t>(peers[q]) * chp + i, npacks))
+              st_plain(ring(peers[q]) + slot * slot_packs + rank * cstride + i, x[u][q]);
         }
       }
       named_barrier(1, nt);
@@ -421,7 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_twoshot_pipe(const __grid_const
 #pragma unroll
         for (int u = 0; u < UR; ++u) {
           const int i = i0 + u * nt;
-          if (i < mlen) {
+          if (i < mlen && NAB_DBG_IDX(mb + i, npacks)) {
             Acc<T> a;
             acc_set(a, x[u][0]);
 #pragma unroll
@@ -467,7 +501,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_twoshot_pipe(const __grid_const
           const int i = i0 + u * nt;
 #pragma unroll
           for (int q = 0; q < WS - 1; ++q)
-            if (i < len[q]) st_plain(dst + tb + static_cast<int64_t>(peers[q]) * chp + i, x[u][q]);
+            if (i < len[q] && NAB_DBG_IDX(tb + static_cast<int64_t>(peers[q]) * chp + i, npacks))
+              st_plain(dst + tb + static_cast<int64_t>(peers[q]) * chp + i, x[u][q]);
         }
       }
       named_barrier(3, nt);
@@ -477,6 +512,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_twoshot_pipe(const __grid_const
       }
     }
   }
+}
+
+template <typename T, int WS>
+__global__ void __launch_bounds__(kThreads, 1) k_twoshot_pipe(const __grid_constant__ ARParams p) {
+  const RankView& me = p.v[blockIdx.y];
+  if (!launch_ok(p, me, WS, pipe_region_ok<WS>(p, blockIdx.x, p.chunk_packs))) return;
+  const uint32_t epoch = begin_call(me);
+  const WaitCtx w = make_wait(p, me, epoch);
+  twoshot_pipe_body<T, WS>(p, me, epoch, w, blockIdx.x, gridDim.x, reinterpret_cast<const uint4*>(me.in),
+                           reinterpret_cast<uint4*>(me.out), p.npacks, p.chunk_packs);
   end_call(me, epoch);
 }
 
@@ -490,6 +535,11 @@ template <typename T>
 __global__ void __launch_bounds__(kThreads) k_hier(const __grid_constant__ ARParams p) {
   constexpr int XW = AccWords<T>::kW;
   const RankView& me = p.v[blockIdx.y];
+  if (!launch_ok(p, me, p.ws, p.gsize * p.ngroups == p.ws && static_cast<int>(blockIdx.x) < p.L.hier_ctas &&
+                                  static_cast<int64_t>(p.chunk_packs) * 16 <= p.L.hier_chunk &&
+                                  p.L.hier_off + static_cast<int64_t>(blockIdx.x + 1) * (p.gsize + 4 * p.ngroups + 1) *
+                                                     p.L.hier_chunk <= p.L.ws_bytes))
+    return;
   const int rank = me.rank;
   const uint32_t epoch = begin_call(me);
   const WaitCtx w = make_wait(p, me, epoch);
@@ -583,6 +633,8 @@ __global__ void __launch_bounds__(kThreads) k_hier(const __grid_constant__ ARPar
 template <typename T, int WS>
 __global__ void __launch_bounds__(kThreads) k_oneshot_pull(const __grid_constant__ ARParams p) {
   const RankView& me = p.v[blockIdx.y];
+  // the RankData slot must lie inside the registry
+  if (!launch_ok(p, me, WS, me.reg != nullptr && me.reg < me.reg_end)) return;
   const int rank = me.rank;
   const uint32_t epoch = begin_call(me);
   const WaitCtx w = make_wait(p, me, epoch);
@@ -617,6 +669,9 @@ template <typename T, int WS>
 __global__ void __launch_bounds__(kThreads, 2) k_nvls_oneshot(const __grid_constant__ ARParams p) {
   constexpr int U = 4;
   const RankView& me = p.v[blockIdx.y];
+  if (!launch_ok(p, me, WS, me.mc != nullptr && blockIdx.x < kMaxBlocks && p.npacks * 16 <= p.L.oneshot_max &&
+                                p.L.mc_oneshot_off + 2 * p.L.oneshot_max <= p.L.mc_bytes))
+    return;
   const uint32_t epoch = begin_call(me);
   const WaitCtx w = make_wait(p, me, epoch);
   const int b = blockIdx.x;
@@ -704,20 +759,18 @@ NAB_DINLINE bool pipe_wait(const uint32_t* ctr, uint32_t target, const WaitCtx& 
   }
 }
 
+// Body of the pipelined NVLS two-shot for CTA c of C on packs [0, npacks)
+// of src/dst (a hybrid launch passes the message's suffix).
 template <typename T, int WS>
-__global__ void __launch_bounds__(kThreads, 1) k_nvls_twoshot(const __grid_constant__ ARParams p) {
+__device__ __forceinline__ void nvls_twoshot_body(const ARParams& p, const RankView& me, uint32_t epoch,
+                                                  const WaitCtx& w, int c, int C, const uint4* src, uint4* dst,
+                                                  int64_t npacks, int chp) {
   constexpr int S = kNvlsSlots;
   constexpr int U = 8;
   constexpr int UL = 8;  // multimem.ld_reduce requests in flight per reducer thread
-  const RankView& me = p.v[blockIdx.y];
   const int rank = me.rank;
-  const uint32_t epoch = begin_call(me);
-  const WaitCtx w = make_wait(p, me, epoch);
-  const int c = blockIdx.x;
-  const int C = gridDim.x;
-  const int chp = p.chunk_packs;
   const int64_t tile = static_cast<int64_t>(WS) * chp;
-  const int64_t ntiles = (p.npacks + tile - 1) / tile;
+  const int64_t ntiles = (npacks + tile - 1) / tile;
   const int64_t my_tiles = ntiles > c ? (ntiles - c + C - 1) / C : 0;
   const int64_t cstride = p.L.nvls_chunk / 16;  // packs between chunks of a slot
   const int64_t slot_packs = WS * cstride;
@@ -726,8 +779,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_nvls_twoshot(const __grid_const
   uint4* mcb = reinterpret_cast<uint4*>(me.mc + cta_off);
   NvlsPad* upad = reinterpret_cast<NvlsPad*>(me.uc);
   NvlsPad* mpad = reinterpret_cast<NvlsPad*>(me.mc);
-  const uint4* src = reinterpret_cast<const uint4*>(me.in);
-  uint4* dst = reinterpret_cast<uint4*>(me.out);
 
   __shared__ uint32_t s_base;
   __shared__ int s_abort;
@@ -761,7 +812,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_nvls_twoshot(const __grid_const
       named_barrier(1, nt);
       if (*abort_flag) break;
       const int64_t tb = (c + k * C) * tile;
-      const int tlen = static_cast<int>(span_len(tile, p.npacks - tb));
+      const int tlen = static_cast<int>(span_len(tile, npacks - tb));
       uint4* us = ucb + slot * slot_packs;
       for (int i0 = t; i0 < tlen; i0 += nt * U) {
         uint4 x[U];
@@ -790,7 +841,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_nvls_twoshot(const __grid_const
       if (*abort_flag) break;
       fence_proxy_alias();  // unicast acquire before multicast loads
       const int64_t mb = (c + k * C) * tile + static_cast<int64_t>(rank) * chp;
-      const int mlen = static_cast<int>(span_len(chp, p.npacks - mb));
+      const int mlen = static_cast<int>(span_len(chp, npacks - mb));
       uint4* mchunk = mcb + slot * slot_packs + rank * cstride;
       for (int i0 = t; i0 < mlen; i0 += nt * UL) {
         uint4 y[UL];
@@ -822,7 +873,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_nvls_twoshot(const __grid_const
       if (*abort_flag) break;
       fence_proxy_alias();  // the owners' multicast stores before unicast loads
       const int64_t tb = (c + k * C) * tile;
-      const int tlen = static_cast<int>(span_len(tile, p.npacks - tb));
+      const int tlen = static_cast<int>(span_len(tile, npacks - tb));
       const uint4* us = ucb + slot * slot_packs;
       for (int i0 = t; i0 < tlen; i0 += nt * U) {
         uint4 x[U];
@@ -846,6 +897,45 @@ __global__ void __launch_bounds__(kThreads, 1) k_nvls_twoshot(const __grid_const
   }
   __syncthreads();
   if (threadIdx.x == 0) upad->pipe_tiles[c] = base + static_cast<uint32_t>(my_tiles);
+}
+
+template <typename T, int WS>
+__global__ void __launch_bounds__(kThreads, 1) k_nvls_twoshot(const __grid_constant__ ARParams p) {
+  const RankView& me = p.v[blockIdx.y];
+  if (!launch_ok(p, me, WS, nvls_region_ok<WS>(p, me, blockIdx.x, p.chunk_packs))) return;
+  const uint32_t epoch = begin_call(me);
+  const WaitCtx w = make_wait(p, me, epoch);
+  nvls_twoshot_body<T, WS>(p, me, epoch, w, blockIdx.x, gridDim.x, reinterpret_cast<const uint4*>(me.in),
+                           reinterpret_cast<uint4*>(me.out), p.npacks, p.chunk_packs);
+  end_call(me, epoch);
+}
+
+// ---------------------------------------------------------------- hybrid ----
+// One launch, two protocols on disjoint parts of the message: CTAs
+// [0, hyb_ctas) run the P2P pipelined two-shot on packs [0, split_packs)
+// (link-bound: 1.75 S per direction of each GPU's NVLink at 8 ranks), the
+// rest run the NVLS two-shot on the remainder (about 1.125 S per direction,
+// bound by the switch's reduction rate). Their rings, flags and counters are
+// disjoint, so they share only the call's epoch.
+template <typename T, int WS>
+__global__ void __launch_bounds__(kThreads, 1) k_hybrid(const __grid_constant__ ARParams p) {
+  const RankView& me = p.v[blockIdx.y];
+  const int cb = static_cast<int>(blockIdx.x);
+  if (!launch_ok(p, me, WS,
+                 p.split_packs > 0 && p.split_packs < p.npacks &&
+                     (cb < p.hyb_ctas ? pipe_region_ok<WS>(p, cb, p.chunk_packs)
+                                      : nvls_region_ok<WS>(p, me, cb - p.hyb_ctas, p.chunk_packs2))))
+    return;
+  const uint32_t epoch = begin_call(me);
+  const WaitCtx w = make_wait(p, me, epoch);
+  const uint4* src = reinterpret_cast<const uint4*>(me.in);
+  uint4* dst = reinterpret_cast<uint4*>(me.out);
+  const int c = blockIdx.x;
+  if (c < p.hyb_ctas)
+    twoshot_pipe_body<T, WS>(p, me, epoch, w, c, p.hyb_ctas, src, dst, p.split_packs, p.chunk_packs);
+  else
+    nvls_twoshot_body<T, WS>(p, me, epoch, w, c - p.hyb_ctas, gridDim.x - p.hyb_ctas, src + p.split_packs,
+                             dst + p.split_packs, p.npacks - p.split_packs, p.chunk_packs2);
   end_call(me, epoch);
 }
 
@@ -860,6 +950,7 @@ cudaError_t launch_ws(int algo, const ARParams& p, dim3 grid, cudaStream_t s, bo
     case kAlgoOneshotPull: fn = reinterpret_cast<void*>(&k_oneshot_pull<T, WS>); break;
     case kAlgoNvlsOneshot: fn = reinterpret_cast<void*>(&k_nvls_oneshot<T, WS>); break;
     case kAlgoNvlsTwoshot: fn = reinterpret_cast<void*>(&k_nvls_twoshot<T, WS>); break;
+    case kAlgoHybrid: fn = reinterpret_cast<void*>(&k_hybrid<T, WS>); break;
     default: return cudaErrorInvalidValue;
   }
   void* args[] = {const_cast<ARParams*>(&p)};

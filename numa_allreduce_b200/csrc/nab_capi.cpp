@@ -119,6 +119,42 @@ NAB_API int nab_allreduce(void* ptr, cudaStream_t stream, const void* input, voi
   return do_allreduce(ptr, stream, input, output, numel, dtype, algo);
 }
 
+// Replaces the automatic choice's steps for one dtype (0 fp32, 1 fp16, 2
+// bf16): n ascending byte limits with their protocol ids, and the protocol of
+// larger messages (100 = NCCL, which this ABI cannot call: such messages take
+// the last custom protocol of the steps). The Python package hands the same
+// steps to its communicators, from its tuning table or the built-in ones.
+NAB_API int nab_set_auto_table(void* ptr, int dtype, int n, const int64_t* max_bytes, const int* algos,
+                               int fallback) {
+  return guarded([&] {
+    if (!ptr) throw std::invalid_argument("null communicator");
+    if (n < 0 || (n > 0 && (!max_bytes || !algos))) throw std::invalid_argument("bad step arrays");
+    nab::AutoTable t;
+    for (int i = 0; i < n; ++i) t.steps.push_back({max_bytes[i], algos[i]});
+    t.fallback = fallback;
+    C(ptr)->set_auto_table(dtype, t);
+  });
+}
+
+// Hybrid protocol split: per mille of each message on the P2P part, and the
+// CTAs of the P2P and NVLS parts.
+NAB_API int nab_set_hybrid(void* ptr, int p2p_permille, int p2p_ctas, int nvls_ctas) {
+  return guarded([&] {
+    if (!ptr) throw std::invalid_argument("null communicator");
+    C(ptr)->set_hybrid(p2p_permille, p2p_ctas, nvls_ctas);
+  });
+}
+
+// The protocol the automatic choice launches for a message (negative on error).
+NAB_API int nab_auto_protocol(void* ptr, int64_t nbytes, int dtype) {
+  int algo = -1;
+  guarded([&] {
+    if (!ptr) throw std::invalid_argument("null communicator");
+    algo = C(ptr)->plan(nbytes, nab::kAlgoAuto, false, dtype).algo;
+  });
+  return algo;
+}
+
 NAB_API uint32_t nab_error_code(void* ptr) { return ptr ? C(ptr)->error_code() : 0u; }
 
 NAB_API int nab_reset(void* ptr) {

@@ -60,7 +60,48 @@ CommConfig config_from_list(const std::vector<int64_t>& v) {
   c.timeout_ns = static_cast<uint64_t>(at(5, static_cast<int64_t>(c.timeout_ns)));
   c.pipe_ctas = static_cast<int>(at(6, c.pipe_ctas));
   c.pipe_tile = at(7, c.pipe_tile);
+  c.hybrid_p2p_permille = static_cast<int>(at(8, c.hybrid_p2p_permille));
+  c.hybrid_p2p_ctas = static_cast<int>(at(9, c.hybrid_p2p_ctas));
+  c.hybrid_nvls_ctas = static_cast<int>(at(10, c.hybrid_nvls_ctas));
   return c;
+}
+
+AutoTable builtin_auto_table(int ws, bool has_nvls) {
+  AutoTable t;
+  if (ws <= 1) {
+    t.steps = {{int64_t(1) << 62, kAlgoCopy}};
+    return t;
+  }
+  // push one-shot for latency-bound sizes, the pipelined store two-shot in the
+  // middle, and on NVSwitch systems with multicast the hybrid (P2P + NVLS in
+  // one launch) for large messages
+  t.steps.push_back({512 << 10, kAlgoOneshot});
+  if (has_nvls) {
+    t.steps.push_back({int64_t(kHybridMinBytes) - 1, kAlgoTwoshotPipe});
+    t.steps.push_back({int64_t(1) << 62, kAlgoHybrid});
+  } else {
+    t.steps.push_back({int64_t(1) << 62, kAlgoTwoshotPipe});
+  }
+  t.fallback = kAlgoNccl;
+  return t;
+}
+
+int choose_auto(const AutoTable& t, int ws, int64_t nbytes, bool has_nvls, bool has_groups) {
+  if (ws <= 1) return kAlgoCopy;
+  int algo = t.fallback;
+  for (const AutoStep& st : t.steps) {
+    if (nbytes <= st.max_bytes) {
+      algo = st.algo;
+      break;
+    }
+  }
+  if (!has_nvls) {
+    if (algo == kAlgoNvlsTwoshot) algo = kAlgoTwoshot;
+    if (algo == kAlgoNvlsOneshot) algo = kAlgoOneshot;
+    if (algo == kAlgoHybrid) algo = kAlgoTwoshotPipe;
+  }
+  if (algo == kAlgoHier && !has_groups) algo = kAlgoTwoshot;
+  return algo;
 }
 
 Layout make_layout(int ws, const CommConfig& cfg) {
@@ -74,6 +115,9 @@ Layout make_layout(int ws, const CommConfig& cfg) {
   if (cfg.pipe_ctas < 1 || cfg.pipe_ctas > kMaxBlocks) throw std::invalid_argument("pipe_ctas must be in [1, 160]");
   if (cfg.pipe_tile < (64 << 10) || cfg.pipe_tile > (4 << 20))
     throw std::invalid_argument("pipe_tile must be in [64 KiB, 4 MiB]");
+  if (cfg.hybrid_p2p_permille < 0 || cfg.hybrid_p2p_permille > 1000 || cfg.hybrid_p2p_ctas < 1 ||
+      cfg.hybrid_p2p_ctas > cfg.pipe_ctas || cfg.hybrid_nvls_ctas < 1 || cfg.hybrid_nvls_ctas > kNvlsCtas)
+    throw std::invalid_argument("hybrid split: permille in [0, 1000], P2P CTAs <= pipe_ctas, NVLS CTAs <= 128");
   Layout L{};
   int64_t off = round_up(static_cast<int64_t>(sizeof(SignalPad)), kAlign);
   L.oneshot_off = off;
@@ -131,6 +175,33 @@ Communicator::Communicator(int rank, int ws, const std::vector<char*>& wsp, void
   NAB_CUDA_CHECK(cudaMemset(err_dev_, 0, sizeof(ErrorState)));
   NAB_CUDA_CHECK(cudaHostAlloc(&err_host_, 64, cudaHostAllocMapped | cudaHostAllocPortable));
   std::memset(err_host_, 0, 64);
+  for (auto& t : auto_) t = builtin_auto_table(ws_, false);
+}
+
+void Communicator::set_auto_table(int dtype, const AutoTable& t) {
+  if (dtype < kF32 || dtype > kBF16) throw std::invalid_argument("dtype must be 0, 1 or 2");
+  int64_t prev = -1;
+  for (const AutoStep& st : t.steps) {
+    if (st.max_bytes <= prev) throw std::invalid_argument("table steps must be strictly ascending");
+    if (st.algo <= kAlgoAuto || (st.algo >= kAlgoCount && st.algo != kAlgoNccl))
+      throw std::invalid_argument("unknown protocol in table: " + std::to_string(st.algo));
+    prev = st.max_bytes;
+  }
+  auto_[dtype] = t;
+}
+
+const AutoTable& Communicator::auto_table(int dtype) const {
+  if (dtype < kF32 || dtype > kBF16) throw std::invalid_argument("dtype must be 0, 1 or 2");
+  return auto_[dtype];
+}
+
+void Communicator::set_hybrid(int p2p_permille, int p2p_ctas, int nvls_ctas) {
+  CommConfig c = cfg_;
+  c.hybrid_p2p_permille = p2p_permille;
+  c.hybrid_p2p_ctas = p2p_ctas;
+  c.hybrid_nvls_ctas = nvls_ctas;
+  make_layout(ws_, c);  // validates; the layout itself does not depend on the split
+  cfg_ = c;
 }
 
 Communicator::~Communicator() {
@@ -165,6 +236,8 @@ void Communicator::attach_nvls(char* mc, char* uc, int64_t bytes) {
   mc_ = mc;
   uc_ = uc;
   mc_bytes_ = bytes;
+  // the built-in steps depend on multicast support; a table set later wins
+  for (auto& t : auto_) t = builtin_auto_table(ws_, true);
 }
 
 RankData* Communicator::reserve_rank_data() {
@@ -232,7 +305,8 @@ void Communicator::register_graph_buffers(const std::vector<std::string>& handle
   graph_unreg_.clear();
 }
 
-LaunchPlan Communicator::plan(int64_t nbytes, int algo, bool registered) const {
+LaunchPlan Communicator::plan(int64_t nbytes, int algo, bool registered, int dtype) const {
+  (void)registered;
   LaunchPlan pl;
   const int64_t npacks = nbytes / 16;
   if (ws_ == 1) {
@@ -241,15 +315,24 @@ LaunchPlan Communicator::plan(int64_t nbytes, int algo, bool registered) const {
     return pl;
   }
   if (algo == kAlgoAuto) {
-    if (registered && nbytes <= cfg_.oneshot_max && nbytes <= (64 << 10))
-      algo = kAlgoOneshotPull;
-    else if (nbytes <= std::min<int64_t>(cfg_.oneshot_max, 256 << 10))
-      algo = kAlgoOneshot;
-    else if (mc_ != nullptr)
-      algo = kAlgoNvlsTwoshot;
-    else
-      algo = kAlgoTwoshot;
+    const AutoTable& t = auto_table(dtype);
+    algo = choose_auto(t, ws_, nbytes, mc_ != nullptr, ngroups_ > 0);
+    if (algo == kAlgoNccl) {
+      // no NCCL here: the last custom protocol of the table takes the message
+      algo = kAlgoTwoshotPipe;
+      for (auto it = t.steps.rbegin(); it != t.steps.rend(); ++it)
+        if (it->algo != kAlgoNccl) {
+          algo = choose_auto(AutoTable{{{int64_t(1) << 62, it->algo}}, kAlgoNccl}, ws_, nbytes, mc_ != nullptr,
+                             ngroups_ > 0);
+          break;
+        }
+    }
+    if ((algo == kAlgoOneshot || algo == kAlgoNvlsOneshot) && nbytes > cfg_.oneshot_max) algo = kAlgoTwoshotPipe;
   }
+  if (algo == kAlgoHybrid && mc_ == nullptr)
+    throw std::invalid_argument("hybrid protocol requested but no multicast workspace attached");
+  // too small to split: the whole message takes the P2P part
+  if (algo == kAlgoHybrid && npacks < 2 * 32 * ws_) algo = kAlgoTwoshotPipe;
   if ((algo == kAlgoNvlsOneshot || algo == kAlgoNvlsTwoshot) && mc_ == nullptr)
     throw std::invalid_argument("NVLS protocol requested but no multicast workspace attached");
   if (algo == kAlgoHier && ngroups_ == 0)
@@ -282,6 +365,29 @@ LaunchPlan Communicator::plan(int64_t nbytes, int algo, bool registered) const {
       pl.rounds = static_cast<int>(per_cta);
       break;
     }
+    case kAlgoHybrid: {
+      // P2P share of the message and CTA budget of each part from the config;
+      // the split point is a multiple of 16 packs (256 B) and both parts are
+      // non-empty
+      const int64_t permille = clampv<int64_t>(cfg_.hybrid_p2p_permille, 1, 999);
+      const int cp_max = cfg_.hybrid_p2p_ctas;
+      const int cn_max = cfg_.hybrid_nvls_ctas;
+      const int64_t split = clampv<int64_t>((npacks * permille / 1000) / 16 * 16, 16, (npacks - 1) / 16 * 16);
+      const int64_t rest = npacks - split;
+      auto part = [&](int64_t n, int64_t cap_bytes, int cmax, int& ctas) {
+        const int64_t chp = std::min(cap_bytes / 16, std::max<int64_t>(32, ceil_div_host(n, ws_ * cmax)));
+        ctas = static_cast<int>(clampv<int64_t>(ceil_div_host(n, ws_ * chp), 1, cmax));
+        return static_cast<int>(chp);
+      };
+      int cp = 0, cn = 0;
+      pl.chunk_packs = part(split, L_.pipe_chunk, cp_max, cp);
+      pl.chunk_packs2 = part(rest, L_.nvls_chunk, cn_max, cn);
+      pl.hyb_ctas = cp;
+      pl.split_packs = split;
+      pl.grid = dim3(static_cast<unsigned>(cp + cn));
+      pl.rounds = 1;
+      break;
+    }
     case kAlgoTwoshot:
     case kAlgoHier: {
       const bool hier = algo == kAlgoHier;
@@ -309,6 +415,7 @@ RankView Communicator::view(const void* in, void* out, const RankData* reg) cons
   v.out = static_cast<char*>(out);
   for (int i = 0; i < ws_; ++i) v.wsp[i] = wsp_[i];
   v.reg = reg;
+  v.reg_end = rd_end_;
   v.mc = mc_;
   v.uc = uc_;
   v.rank = rank_;
@@ -323,6 +430,9 @@ void Communicator::fill_params(ARParams& p, const LaunchPlan& pl, int64_t nbytes
   p.ws = ws_;
   p.chunk_packs = pl.chunk_packs;
   p.rounds = pl.rounds;
+  p.hyb_ctas = pl.hyb_ctas;
+  p.chunk_packs2 = pl.chunk_packs2;
+  p.split_packs = pl.split_packs;
   p.ngroups = ngroups_;
   p.gsize = gsize_;
   std::memcpy(p.group_of, group_of_, sizeof(group_of_));
@@ -340,7 +450,7 @@ int Communicator::allreduce(cudaStream_t s, const void* in, void* out, int64_t n
   if (reinterpret_cast<uintptr_t>(in) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
     throw std::invalid_argument("allreduce buffers must be 16-byte aligned");
   if (ws_ == 1 && in == out) return kAlgoCopy;  // nothing to do
-  const LaunchPlan pl = plan(nbytes, algo, registered);
+  const LaunchPlan pl = plan(nbytes, algo, registered, dtype);
   const RankData* reg = nullptr;
   if (pl.algo == kAlgoOneshotPull) {
     auto it = buffers_.find(in);
@@ -386,9 +496,11 @@ void Communicator::reset() {
   std::memset(err_host_, 0, 64);
 }
 
-int emulate_allreduce(const std::vector<Communicator*>& comms, cudaStream_t s,
-                      const std::vector<const void*>& ins, const std::vector<void*>& outs,
-                      int64_t nbytes, int dtype, int algo, int participants) {
+namespace {
+
+int emulate_impl(const std::vector<Communicator*>& comms, cudaStream_t s, const std::vector<const void*>& ins,
+                 const std::vector<void*>& outs, int64_t nbytes, int dtype, int algo, int participants,
+                 bool bad_rank) {
   const int ws = static_cast<int>(comms.size());
   if (participants < 0) participants = ws;
   if (participants < 1 || participants > ws) throw std::invalid_argument("bad participant count");
@@ -397,8 +509,8 @@ int emulate_allreduce(const std::vector<Communicator*>& comms, cudaStream_t s,
     throw std::invalid_argument("emulation needs 2..8 communicators and one buffer per rank");
   if (nbytes <= 0 || nbytes % 16 != 0)
     throw std::invalid_argument("allreduce size must be a positive multiple of 16 bytes");
-  if (algo == kAlgoNvlsOneshot || algo == kAlgoNvlsTwoshot || algo == kAlgoOneshotPull)
-    throw std::invalid_argument("NVLS and pull protocols cannot be emulated on one GPU");
+  if (algo == kAlgoNvlsOneshot || algo == kAlgoNvlsTwoshot || algo == kAlgoOneshotPull || algo == kAlgoHybrid)
+    throw std::invalid_argument("NVLS, hybrid and pull protocols cannot be emulated on one GPU");
   Communicator* c0 = comms[0];
   LaunchPlan pl = c0->plan(nbytes, algo, false);
   // Every CTA of every emulated rank must be resident at once: cap the grid
@@ -429,6 +541,7 @@ int emulate_allreduce(const std::vector<Communicator*>& comms, cudaStream_t s,
     if (comms[r]->rank() != r) throw std::invalid_argument("communicators must be in rank order");
     p.v[r] = comms[r]->view(ins[r], outs[r], nullptr);
   }
+  if (bad_rank) p.v[0].rank = ws;  // caught by the device bounds check of debug builds
   pl.grid.y = participants;
   const cudaError_t e = launch_allreduce(pl.algo, dtype, p, pl.grid, s, true);
   if (e != cudaSuccess)
@@ -436,6 +549,22 @@ int emulate_allreduce(const std::vector<Communicator*>& comms, cudaStream_t s,
   for (int r = 0; r < participants; ++r) comms[r]->count_launch();
   return pl.algo;
 }
+
+}  // namespace
+
+int emulate_allreduce(const std::vector<Communicator*>& comms, cudaStream_t s,
+                      const std::vector<const void*>& ins, const std::vector<void*>& outs,
+                      int64_t nbytes, int dtype, int algo, int participants) {
+  return emulate_impl(comms, s, ins, outs, nbytes, dtype, algo, participants, false);
+}
+
+#if NAB_DEBUG_BOUNDS
+int emulate_allreduce_bad_rank(const std::vector<Communicator*>& comms, cudaStream_t s,
+                               const std::vector<const void*>& ins, const std::vector<void*>& outs,
+                               int64_t nbytes, int dtype, int algo) {
+  return emulate_impl(comms, s, ins, outs, nbytes, dtype, algo, -1, true);
+}
+#endif
 
 void* ipc_alloc_shared(size_t bytes, cudaStream_t s, std::string* handle_out) {
   void* buf = nullptr;

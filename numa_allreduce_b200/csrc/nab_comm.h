@@ -20,6 +20,7 @@
 #include <vector>
 
 #include "nab_common.h"
+#include "nab_device_flags.h"
 #include "nab_params.h"
 
 namespace nab {
@@ -35,11 +36,38 @@ struct CommConfig {
   uint64_t timeout_ns = 5000000000ull;
   int pipe_ctas = kPipeCtas;             // CTAs of the pipelined two-shot
   int64_t pipe_tile = kPipeTileBytes;    // bytes per ring slot of the pipelined two-shot
+  // Hybrid protocol: share of the message (per mille) that takes the P2P
+  // two-shot, and the CTA budget of each part (the rest goes through NVLS).
+  int hybrid_p2p_permille = kHybridP2pPermille;
+  int hybrid_p2p_ctas = kHybridP2pCtas;
+  int hybrid_nvls_ctas = kHybridNvlsCtas;
 };
 
 // Config from a flat list: [oneshot_max, chunk_max, max_ctas, oneshot_ctas,
-// fused_bytes, timeout_ns, pipe_ctas, pipe_tile]; missing entries keep defaults.
+// fused_bytes, timeout_ns, pipe_ctas, pipe_tile, hybrid_p2p_permille,
+// hybrid_p2p_ctas, hybrid_nvls_ctas]; missing entries keep defaults.
 CommConfig config_from_list(const std::vector<int64_t>& v);
+
+// Protocol steps of the automatic choice for one dtype: the first step whose
+// max_bytes >= the message size gives the protocol; a larger message gets
+// `fallback` (kAlgoNccl: the caller should use NCCL). The Python selector
+// (parallel/select.py) loads the same table and hands it to the communicator,
+// so both make the same choice; without a table both use builtin_auto_table().
+struct AutoStep {
+  int64_t max_bytes;
+  int algo;
+};
+struct AutoTable {
+  std::vector<AutoStep> steps;
+  int fallback = kAlgoNccl;
+};
+
+// Built-in steps for a world size (used when no measured table covers it).
+AutoTable builtin_auto_table(int ws, bool has_nvls);
+// The protocol the table picks, after substituting what this communicator
+// cannot run (NVLS and hybrid need a multicast workspace, hier needs groups).
+// kAlgoNccl means "use NCCL"; kAlgoCopy for world size 1.
+int choose_auto(const AutoTable& t, int ws, int64_t nbytes, bool has_nvls, bool has_groups);
 
 // Computes where everything lives in the IPC and NVLS workspaces.
 Layout make_layout(int ws, const CommConfig& cfg);
@@ -49,6 +77,9 @@ struct LaunchPlan {
   dim3 grid{1, 1, 1};
   int chunk_packs = 0;
   int rounds = 0;
+  int hyb_ctas = 0;       // hybrid only
+  int chunk_packs2 = 0;
+  int64_t split_packs = 0;
 };
 
 class Communicator {
@@ -69,6 +100,12 @@ class Communicator {
   bool has_nvls() const { return mc_ != nullptr; }
   bool has_groups() const { return ngroups_ > 0; }
 
+  // Replaces the automatic-choice table of one dtype (kF32/kF16/kBF16).
+  void set_auto_table(int dtype, const AutoTable& t);
+  const AutoTable& auto_table(int dtype) const;
+  // Changes the hybrid protocol's split at run time (tuning sweeps).
+  void set_hybrid(int p2p_permille, int p2p_ctas, int nvls_ctas);
+
   // Hierarchical groups: equal-size partition of the ranks.
   void set_groups(const std::vector<std::vector<int>>& groups);
   // NVLS workspace: multicast VA and this rank's own unicast VA of it.
@@ -84,8 +121,10 @@ class Communicator {
                               const std::vector<std::vector<int64_t>>& offsets);
   size_t num_graph_buffers() const { return graph_unreg_.size(); }
 
-  // Chooses the protocol when algo == kAlgoAuto and sizes the launch.
-  LaunchPlan plan(int64_t nbytes, int algo, bool registered) const;
+  // Chooses the protocol when algo == kAlgoAuto and sizes the launch. A
+  // message the table hands to NCCL gets the table's last custom protocol
+  // here: a caller of the C ABI has no NCCL to fall back to.
+  LaunchPlan plan(int64_t nbytes, int algo, bool registered, int dtype = kBF16) const;
   // Fills the view of this rank for a launch.
   RankView view(const void* in, void* out, const RankData* reg) const;
   // Fills everything but the views.
@@ -131,6 +170,7 @@ class Communicator {
   int8_t group_of_[kMaxRanks] = {};
   int8_t lidx_of_[kMaxRanks] = {};
   int8_t member_[kMaxRanks][kMaxRanks] = {};
+  AutoTable auto_[3];  // per dtype
   RankData* rd_base_;
   RankData* rd_cur_;
   RankData* rd_end_;
@@ -149,6 +189,15 @@ class Communicator {
 int emulate_allreduce(const std::vector<Communicator*>& comms, cudaStream_t s,
                       const std::vector<const void*>& ins, const std::vector<void*>& outs,
                       int64_t nbytes, int dtype, int algo, int participants = -1);
+
+#if NAB_DEBUG_BOUNDS
+// Debug builds only: the same launch with emulated rank 0's view claiming an
+// out-of-range rank, so that the device bounds check must catch it before
+// that rank touches any memory (tests of the check itself).
+int emulate_allreduce_bad_rank(const std::vector<Communicator*>& comms, cudaStream_t s,
+                               const std::vector<const void*>& ins, const std::vector<void*>& outs,
+                               int64_t nbytes, int dtype, int algo);
+#endif
 
 // Legacy CUDA IPC helpers (reference src/numa_all_reduce.cu:693-734).
 void* ipc_alloc_shared(size_t bytes, cudaStream_t s, std::string* handle_out);

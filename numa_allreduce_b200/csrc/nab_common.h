@@ -32,7 +32,9 @@ enum Algo : int {
   kAlgoOneshotPull = 6,  // registered inputs: read peers' buffers directly
   kAlgoCopy = 7,         // world size 1: out = in
   kAlgoTwoshotPipe = 8,  // two-shot, warp-specialised and pipelined over a slot ring
-  kAlgoCount = 9,
+  kAlgoHybrid = 9,       // one launch: P2P pipelined two-shot on a prefix, NVLS two-shot on the rest
+  kAlgoCount = 10,
+  kAlgoNccl = 100,       // selector result only: the caller should use NCCL
 };
 
 // Error codes written into ErrorState::code by device code.
@@ -54,6 +56,9 @@ enum Stage : uint32_t {
   kStageNvls2 = 8,
   kStageFused = 9,
   kStageGemmAR = 10,
+  kStageGemm = 11,       // plain GEMM: its own TMA / tensor-core mbarriers
+  kStageAttn = 12,       // decode attention: its own bulk-copy mbarriers
+  kStageBounds = 13,     // debug builds: an index failed a bounds check
 };
 
 // Lives in host-mapped pinned memory so the host can read it at any time, even
@@ -138,6 +143,15 @@ constexpr int64_t kPipeTileBytes = 256 << 10;
 constexpr int kNvlsSlots = 4;
 constexpr int kNvlsCtas = 128;
 constexpr int64_t kNvlsTileBytes = 256 << 10;  // one ring slot: ws chunks
+
+// Default split of the hybrid protocol (P2P share of the message in per
+// mille, CTAs of each part; their sum stays below the 148 SMs so every CTA of
+// the launch is resident at once).
+constexpr int kHybridP2pPermille = 400;
+constexpr int kHybridP2pCtas = 64;
+constexpr int kHybridNvlsCtas = 80;
+// Smallest message the built-in steps give to the hybrid protocol.
+constexpr int64_t kHybridMinBytes = int64_t(32) << 20;
 
 constexpr uint64_t kSeqShift = 20;  // rounds per call < 2^20
 

@@ -18,6 +18,12 @@
 
 #define NAB_DINLINE __device__ __forceinline__
 
+// Debug builds (-DNAB_DEBUG_BOUNDS=1) check launch parameters, slot capacity,
+// ranks and pack indices on the device; a violation is recorded (code
+// kErrBadLaunch, stage kStageBounds) and the guarded access is skipped. No
+// trap, no assert. Release builds compile the checks away.
+#include "nab_device_flags.h"
+
 namespace nab {
 
 // ---------------------------------------------------------------- packs ----
@@ -272,6 +278,33 @@ NAB_DINLINE void record_failure(const WaitCtx& w, uint32_t code, uint32_t peer, 
   }
   atomicAdd(&w.err->count, 1u);
   st_volatile_u32(w.abort, 1u);
+}
+
+// Records a failure of a kernel that has no communicator (no peers to stop):
+// the first one fills the record, later ones only bump the count.
+NAB_DINLINE void record_local_failure(ErrorState* err, uint32_t* err_host, uint32_t code, uint32_t stage,
+                                      uint32_t observed) {
+  if (err == nullptr) return;
+  if (atomicCAS(&err->code, 0u, code) == 0u) {
+    err->rank = 0xffffffffu;
+    err->peer = 0xffffffffu;
+    err->stage = stage;
+    err->block = blockIdx.x + gridDim.x * blockIdx.y;
+    err->epoch = 0;
+    err->observed = observed;
+    __threadfence_system();
+    if (err_host) st_volatile_u32(err_host, code);
+  }
+  atomicAdd(&err->count, 1u);
+}
+
+// Debug builds: true if `cond` holds; otherwise records the violation (with
+// `observed`, e.g. the offending index) and returns false. Always true in
+// release builds.
+NAB_DINLINE bool dbg_ok(bool cond, ErrorState* err, uint32_t* err_host, uint32_t observed) {
+  if (!NAB_DEBUG_BOUNDS || cond) return true;
+  record_local_failure(err, err_host, kErrBadLaunch, kStageBounds, observed);
+  return false;
 }
 
 // Spins until *addr >= target (wrap-safe). Returns false, after recording the

@@ -48,6 +48,7 @@
 #include "nab_driver.h"
 #include "nab_fused.h"
 #include "nab_gemm.h"
+#include "nab_kerr.h"
 #include "nab_proto.cuh"
 #include "nab_sm100.cuh"
 
@@ -153,10 +154,17 @@ __global__ void __launch_bounds__(kGemmThreads, GemmCfg<BN>::kCtasPerSm)
   sm100::tc_fence_after();
   const uint32_t tmem = s_tmem;
 
+  // A wait that ran out: the fused kernel records on its communicator (and
+  // stops this rank's other waits), the plain one on the device's kernel
+  // error record.
   auto fail = [&](uint32_t stage) {
-    if (g.err != nullptr && !*abort_flag) {
-      WaitCtx w = make_wait(g.err, g.err_host, g.timeout_ns, g.wsp, g.rank, 0);
-      record_failure(w, kErrTimeout, static_cast<uint32_t>(g.rank), stage, 0);
+    if (!*abort_flag) {
+      if (g.fused) {
+        WaitCtx w = make_wait(g.err, g.err_host, g.timeout_ns, g.wsp, g.rank, 0);
+        record_failure(w, kErrTimeout, static_cast<uint32_t>(g.rank), stage, 0);
+      } else {
+        record_local_failure(g.err, g.err_host, kErrTimeout, stage, 0);
+      }
     }
     *abort_flag = 1;
   };
@@ -184,7 +192,7 @@ __global__ void __launch_bounds__(kGemmThreads, GemmCfg<BN>::kCtasPerSm)
       for (int i = pre; i < nkb; ++i) {
         const int s = i % S;
         if (!sm100::mbar_wait(&empty_bar[s], ((i / S) - 1) & 1, g.timeout_ns, abort_flag)) {
-          fail(kStageGemmAR);
+          fail(g.fused ? kStageGemmAR : kStageGemm);
           break;
         }
         if (*abort_flag) break;
@@ -208,7 +216,7 @@ __global__ void __launch_bounds__(kGemmThreads, GemmCfg<BN>::kCtasPerSm)
       for (int i = 0; i < nkb; ++i) {
         const int s = i % S;
         if (!sm100::mbar_wait(&full_bar[s], (i / S) & 1, g.timeout_ns, abort_flag)) {
-          fail(kStageGemmAR);
+          fail(g.fused ? kStageGemmAR : kStageGemm);
           break;
         }
         sm100::tc_fence_after();
@@ -228,7 +236,7 @@ __global__ void __launch_bounds__(kGemmThreads, GemmCfg<BN>::kCtasPerSm)
     // [token][feature]; a split with no k-blocks contributes zeros.
     const int q = warp & 3;        // TMEM lane quarter this warp may access
     const int row = q * 32 + lane;  // feature within the tile
-    if (nkb > 0 && !sm100::mbar_wait(&accum_bar, 0, g.timeout_ns, abort_flag)) fail(kStageGemmAR);
+    if (nkb > 0 && !sm100::mbar_wait(&accum_bar, 0, g.timeout_ns, abort_flag)) fail(g.fused ? kStageGemmAR : kStageGemm);
     sm100::tc_fence_after();
     float* acc = reinterpret_cast<float*>(smem);
 #pragma unroll 1
@@ -549,7 +557,10 @@ void gemm_bf16(cudaStream_t s, const void* wt, const void* x, void* y, int T, in
   g.n_tiles = (T + bn - 1) / bn;
   set_splits(g, splits > 0 ? splits : gemm_splits_for(T, N, K, sm_count()), bn);
   g.out = static_cast<__nv_bfloat16*>(y);
-  g.timeout_ns = 2000000000ull;
+  const KernelErrorRecord rec = kernel_error_record();
+  g.err = rec.dev;
+  g.err_host = rec.host;
+  g.timeout_ns = kernel_timeout_ns();
   launch(wt, x, g, bn, s);
 }
 

@@ -19,6 +19,7 @@
 
 #include "nab_device.cuh"
 #include "nab_driver.h"
+#include "nab_kerr.h"
 #include "nab_llama.h"
 #include "nab_sm100.cuh"
 
@@ -73,6 +74,9 @@ struct AttnArgs {
   int q_stride;
   int Hq, Hkv, Lmax, splits;
   float scale;
+  ErrorState* err;         // the device's kernel error record
+  uint32_t* err_host;
+  uint64_t timeout_ns;
 };
 
 NAB_DINLINE uint2 pack4(const float (&f)[4]) {
@@ -240,8 +244,12 @@ __global__ void __launch_bounds__(256) k_attn(const __grid_constant__ AttnArgs a
   int consumed = 0;
   for (int i = 0; i < nchunks; ++i) {
     const int c0 = beg + i * kChunk, n = min(kChunk, end - c0);
-    if (!sm100::mbar_wait(&full_bar[i & 1], (i >> 1) & 1, 1000000000ull, abort_flag)) *abort_flag = 1;
-    else consumed = i + 1;
+    if (!sm100::mbar_wait(&full_bar[i & 1], (i >> 1) & 1, a.timeout_ns, abort_flag)) {
+      if (!*abort_flag) record_local_failure(a.err, a.err_host, kErrTimeout, kStageAttn, static_cast<uint32_t>(i));
+      *abort_flag = 1;
+    } else {
+      consumed = i + 1;
+    }
     const __nv_bfloat16* sk = kv_tile(i & 1, 0);
     const __nv_bfloat16* sv = kv_tile(i & 1, 1);
     if (owns_pos && warp == 0 && g == 0 && pos >= c0 && pos < c0 + n) {
@@ -274,7 +282,7 @@ __global__ void __launch_bounds__(256) k_attn(const __grid_constant__ AttnArgs a
   if (*abort_flag && threadIdx.x == 0) {
     // let copies still in flight land before the CTA's memory goes away
     volatile int never = 0;
-    for (int i = consumed; i < issued; ++i) sm100::mbar_wait(&full_bar[i & 1], (i >> 1) & 1, 1000000000ull, &never);
+    for (int i = consumed; i < issued; ++i) sm100::mbar_wait(&full_bar[i & 1], (i >> 1) & 1, a.timeout_ns, &never);
   }
   // merge the four groups' running states (xor 8, then 16)
   if (warp < G) {
@@ -394,6 +402,13 @@ void launch_attn(cudaStream_t s, const AttnArgs& a, int B) {
   if (e != cudaSuccess) throw std::runtime_error(std::string("attention launch failed: ") + cudaGetErrorString(e));
 }
 
+void set_error_record(AttnArgs& a) {
+  const KernelErrorRecord rec = kernel_error_record();
+  a.err = rec.dev;
+  a.err_host = rec.host;
+  a.timeout_ns = kernel_timeout_ns();
+}
+
 void check_attn(int Hq, int Hkv, int splits) {
   if (Hkv < 1 || Hq % Hkv != 0 || Hq / Hkv > 8) throw std::invalid_argument("attention: need Hq / Hkv <= 8");
   if (splits < 1 || splits > kMaxAttnSplits) throw std::invalid_argument("attention: splits must be in [1, 16]");
@@ -416,6 +431,7 @@ void decode_attention(cudaStream_t s, const void* q, const void* k_cache, const 
   a.Lmax = Lmax;
   a.splits = splits;
   a.scale = 1.f / sqrtf(static_cast<float>(kHeadDim));
+  set_error_record(a);
   launch_attn<false>(s, a, B);
 }
 
@@ -436,6 +452,7 @@ void rope_attention(cudaStream_t s, const void* qkv, const float* cos_t, const f
   a.Lmax = Lmax;
   a.splits = splits;
   a.scale = 1.f / sqrtf(static_cast<float>(kHeadDim));
+  set_error_record(a);
   launch_attn<true>(s, a, B);
 }
 

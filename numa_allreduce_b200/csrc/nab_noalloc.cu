@@ -1,8 +1,10 @@
-// Allocation-free entry point (no counterpart in the reference).
+// Allocation-free entry point (no counterpart in the reference); declared in
+// nab_noalloc.h.
 //
 //   int nab_noalloc_emulated_allreduce(const void* const* inputs,
 //                                      void* const* outputs, int world_size,
 //                                      int64_t numel, int dtype, void* stream);
+//   int nab_noalloc_last_error(uint32_t* record);
 //
 // Runs the two-shot allreduce kernel for `world_size` ranks whose buffers all
 // live on the current GPU (the same single-GPU emulation the library's tests
@@ -29,9 +31,15 @@
 //   clears the signal pads and the error record on its stream first. Calls
 //   that overlap on the GPU (different streams, or different host threads on
 //   the same device without ordering) race on the array; order them.
-// * Returns 0 on success, 1 for a rejected argument, 2 when the world size
+// * The return code covers the argument checks and the launch only: 0 when
+//   the kernel was launched, 1 for a rejected argument, 2 when the world size
 //   needs more scratch than the static array holds, 3 for a CUDA error; a
 //   one-line reason goes to stderr (formatted in a fixed buffer, no heap).
+//   A bounded wait inside the kernel that gives up (after NAB_TIMEOUT_NS,
+//   default 5 s, read from the environment on every call) leaves the output
+//   partly written and records the failure in the array's error record;
+//   nab_noalloc_last_error copies that record out after the caller has
+//   synchronized the stream.
 // * numel * element size must be a positive multiple of 16 bytes and every
 //   pointer 16-byte aligned; dtype is 0 (fp32), 1 (fp16) or 2 (bf16).
 #include <cuda_runtime.h>
@@ -41,12 +49,15 @@
 #include <cstdio>
 #include <mutex>
 
+#include <cstdlib>
+
 #include "nab_kernels.h"
+#include "nab_noalloc.h"
 #include "nab_params.h"
 
 namespace {
 
-constexpr size_t kNoAllocScratchBytes = size_t(12) << 20;
+constexpr size_t kNoAllocScratchBytes = NAB_NOALLOC_SCRATCH_BYTES;
 constexpr int kNoAllocMaxCtas = 8;              // CTAs per emulated rank
 constexpr int64_t kNoAllocChunk = 16 << 10;     // bytes per owner chunk per round
 constexpr int64_t kHeaderBytes = 4096;          // error record
@@ -69,6 +80,18 @@ int fail(int code, const char* fmt, ...) {
 }
 
 int64_t round_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
+
+// Bound of every device-side wait: NAB_TIMEOUT_NS if set (getenv and strtoull
+// allocate nothing), else 5 s.
+uint64_t timeout_ns() {
+  const char* v = std::getenv("NAB_TIMEOUT_NS");
+  if (v != nullptr && *v != '\0') {
+    char* end = nullptr;
+    const unsigned long long t = std::strtoull(v, &end, 0);
+    if (end != v && t > 0) return static_cast<uint64_t>(t);
+  }
+  return 5000000000ull;
+}
 
 }  // namespace
 
@@ -138,7 +161,7 @@ extern "C" __attribute__((visibility("default"))) int nab_noalloc_emulated_allre
   p.err = reinterpret_cast<ErrorState*>(base);
   p.err_host = nullptr;
   p.npacks = npacks;
-  p.timeout_ns = 5000000000ull;
+  p.timeout_ns = timeout_ns();
   p.ws = world_size;
   p.chunk_packs = static_cast<int>(chp);
   p.rounds = static_cast<int>(rounds);
@@ -155,5 +178,24 @@ extern "C" __attribute__((visibility("default"))) int nab_noalloc_emulated_allre
   e = launch_allreduce(kAlgoTwoshot, dtype, p, dim3(static_cast<unsigned>(C), static_cast<unsigned>(world_size)), s,
                        /*cooperative=*/true);
   if (e != cudaSuccess) return fail(kCudaError, "launch failed: %s", cudaGetErrorString(e));
+  return kOk;
+}
+
+extern "C" __attribute__((visibility("default"))) int nab_noalloc_last_error(uint32_t* record) {
+  static_assert(sizeof(nab::ErrorState) == 8 * sizeof(uint32_t), "record layout");
+  if (record == nullptr) return fail(kBadArgument, "record must not be null");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(kCudaError, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(kBadArgument, "device ordinal %d out of range", dev);
+  char* base;
+  {
+    std::lock_guard<std::mutex> lock(g_setup_mu);
+    base = g_scratch_addr[dev];
+  }
+  if (base == nullptr) return kBadArgument;  // no call on this device yet: nothing recorded
+  // the error record sits at the start of the array (see the layout above)
+  e = cudaMemcpy(record, base, sizeof(nab::ErrorState), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return fail(kCudaError, "reading the error record failed: %s", cudaGetErrorString(e));
   return kOk;
 }

@@ -18,6 +18,7 @@ struct RankView {
   char* out;
   char* wsp[kMaxRanks];  // IPC workspace base of every rank, as mapped here
   const RankData* reg;   // peers' registered input pointers (pull protocol)
+  const RankData* reg_end;  // end of this rank's RankData registry (debug bounds checks)
   char* mc;              // multicast address of the NVLS workspace (or null)
   char* uc;              // this rank's own unicast view of the NVLS workspace
   int rank;
@@ -59,7 +60,10 @@ struct ARParams {
   int rounds;            // rounds per CTA
   int ngroups;           // hierarchical: number of groups
   int gsize;             // hierarchical: ranks per group
-  int pad_;
+  int hyb_ctas;          // hybrid: CTAs [0, hyb_ctas) run the P2P part
+  int chunk_packs2;      // hybrid: packs per owner chunk of the NVLS part
+  int pad3_;
+  int64_t split_packs;   // hybrid: packs [0, split_packs) go P2P, the rest NVLS
   int8_t group_of[kMaxRanks];
   int8_t lidx_of[kMaxRanks];
   int8_t member[kMaxRanks][kMaxRanks];  // [group][local index] -> rank

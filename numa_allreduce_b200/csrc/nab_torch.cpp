@@ -15,11 +15,13 @@
 
 #include <stdexcept>
 #include <string>
+#include <tuple>
 #include <vector>
 
 #include "nab_comm.h"
 #include "nab_fused.h"
 #include "nab_gemm.h"
+#include "nab_kerr.h"
 #include "nab_llama.h"
 #include "nab_nvls.h"
 
@@ -121,14 +123,64 @@ void all_reduce_algo(fptr_t fa, const at::Tensor& inp, at::Tensor& out, int64_t 
                    dtype_of(inp), static_cast<int>(algo), registered);
 }
 
-int64_t plan_algo(fptr_t fa, int64_t nbytes, int64_t algo, bool registered) {
+int64_t plan_algo(fptr_t fa, int64_t nbytes, int64_t algo, bool registered, int64_t dtype) {
   if (C(fa)->world_size() == 1) return nab::kAlgoCopy;
-  return C(fa)->plan(nbytes, static_cast<int>(algo), registered).algo;
+  return C(fa)->plan(nbytes, static_cast<int>(algo), registered, static_cast<int>(dtype)).algo;
 }
 
-std::vector<int64_t> plan(fptr_t fa, int64_t nbytes, int64_t algo, bool registered) {
-  const nab::LaunchPlan p = C(fa)->plan(nbytes, static_cast<int>(algo), registered);
-  return {p.algo, p.grid.x, p.chunk_packs, p.rounds};
+std::vector<int64_t> plan(fptr_t fa, int64_t nbytes, int64_t algo, bool registered, int64_t dtype) {
+  const nab::LaunchPlan p = C(fa)->plan(nbytes, static_cast<int>(algo), registered, static_cast<int>(dtype));
+  return {p.algo, p.grid.x, p.chunk_packs, p.rounds, p.hyb_ctas, p.chunk_packs2, p.split_packs};
+}
+
+nab::AutoTable make_table(const std::vector<int64_t>& limits, const std::vector<int64_t>& algos, int64_t fallback) {
+  TORCH_CHECK(limits.size() == algos.size(), "one protocol per step");
+  nab::AutoTable t;
+  for (size_t i = 0; i < limits.size(); ++i) t.steps.push_back({limits[i], static_cast<int>(algos[i])});
+  t.fallback = static_cast<int>(fallback);
+  return t;
+}
+
+void set_auto_table(fptr_t fa, int64_t dtype, const std::vector<int64_t>& limits, const std::vector<int64_t>& algos,
+                    int64_t fallback) {
+  C(fa)->set_auto_table(static_cast<int>(dtype), make_table(limits, algos, fallback));
+}
+
+std::tuple<std::vector<int64_t>, std::vector<int64_t>, int64_t> table_lists(const nab::AutoTable& t) {
+  std::vector<int64_t> limits, algos;
+  for (const auto& st : t.steps) {
+    limits.push_back(st.max_bytes);
+    algos.push_back(st.algo);
+  }
+  return {limits, algos, t.fallback};
+}
+
+std::tuple<std::vector<int64_t>, std::vector<int64_t>, int64_t> get_auto_table(fptr_t fa, int64_t dtype) {
+  return table_lists(C(fa)->auto_table(static_cast<int>(dtype)));
+}
+
+std::tuple<std::vector<int64_t>, std::vector<int64_t>, int64_t> builtin_auto_table(int64_t ws, bool has_nvls) {
+  return table_lists(nab::builtin_auto_table(static_cast<int>(ws), has_nvls));
+}
+
+int64_t choose_auto(int64_t ws, int64_t nbytes, bool has_nvls, bool has_groups, const std::vector<int64_t>& limits,
+                    const std::vector<int64_t>& algos, int64_t fallback) {
+  return nab::choose_auto(make_table(limits, algos, fallback), static_cast<int>(ws), nbytes, has_nvls, has_groups);
+}
+
+// Error record of the kernels without a communicator (GEMM, attention) on the
+// current device: [code, rank, peer, stage, block, epoch, observed, count].
+std::vector<int64_t> kernel_error_state() {
+  const nab::ErrorState st = nab::kernel_error_state();
+  return {st.code, st.rank, st.peer, st.stage, st.block, st.epoch, st.observed, st.count};
+}
+
+int64_t kernel_error_code() { return nab::kernel_error_code(); }
+
+void kernel_error_reset() { nab::kernel_error_reset(); }
+
+void set_hybrid(fptr_t fa, int64_t permille, int64_t p2p_ctas, int64_t nvls_ctas) {
+  C(fa)->set_hybrid(static_cast<int>(permille), static_cast<int>(p2p_ctas), static_cast<int>(nvls_ctas));
 }
 
 void emulate_all_reduce(const std::vector<int64_t>& fas, const std::vector<at::Tensor>& ins,
@@ -150,6 +202,28 @@ void emulate_all_reduce(const std::vector<int64_t>& fas, const std::vector<at::T
   nab::emulate_allreduce(cs, stream, in_ptrs, out_ptrs, ins[0].numel() * ins[0].element_size(),
                          dtype_of(ins[0]), static_cast<int>(algo), static_cast<int>(participants));
 }
+
+#if NAB_DEBUG_BOUNDS
+void debug_emulate_bad_rank(const std::vector<int64_t>& fas, const std::vector<at::Tensor>& ins,
+                            const std::vector<at::Tensor>& outs, int64_t algo) {
+  TORCH_CHECK(fas.size() == ins.size() && ins.size() == outs.size(), "one tensor pair per rank");
+  std::vector<Communicator*> cs;
+  std::vector<const void*> in_ptrs;
+  std::vector<void*> out_ptrs;
+  for (size_t i = 0; i < fas.size(); ++i) {
+    check_io(ins[i], outs[i]);
+    cs.push_back(C(fas[i]));
+    in_ptrs.push_back(ins[i].data_ptr());
+    out_ptrs.push_back(outs[i].data_ptr());
+  }
+  const at::cuda::OptionalCUDAGuard guard(ins[0].device());
+  auto stream = at::cuda::getCurrentCUDAStream().stream();
+  nab::emulate_allreduce_bad_rank(cs, stream, in_ptrs, out_ptrs, ins[0].numel() * ins[0].element_size(),
+                                  dtype_of(ins[0]), static_cast<int>(algo));
+}
+#endif
+
+bool debug_bounds_build() { return NAB_DEBUG_BOUNDS != 0; }
 
 std::tuple<std::vector<int64_t>, std::vector<int64_t>> get_graph_buffer_ipc_meta(fptr_t fa) {
   auto [handles, offsets] = C(fa)->graph_buffer_ipc_meta();
@@ -399,7 +473,8 @@ void silu_mul_op(const at::Tensor& gu, at::Tensor& out) {
 
 TORCH_LIBRARY(nab, m) {
   m.def("meta_size() -> int", &meta_size);
-  // cfg: [oneshot_max, chunk_max, max_ctas, oneshot_ctas, fused_bytes, timeout_ns, pipe_ctas, pipe_tile]
+  // cfg: [oneshot_max, chunk_max, max_ctas, oneshot_ctas, fused_bytes, timeout_ns, pipe_ctas, pipe_tile,
+  //       hybrid_p2p_permille, hybrid_p2p_ctas, hybrid_nvls_ctas]
   m.def("layout(int ws, int[] cfg) -> int[]", &layout);
   m.def("init(int[] ws_ptrs, Tensor rank_data, int rank, bool full_nvlink, int[] cfg) -> int", &init);
   m.def("dispose(int fa) -> ()", &dispose);
@@ -410,8 +485,22 @@ TORCH_LIBRARY(nab, m) {
   m.impl("all_reduce", c10::kCUDA, &all_reduce);
   m.def("all_reduce_algo(int fa, Tensor inp, Tensor(a!) out, int algo, bool registered) -> ()");
   m.impl("all_reduce_algo", c10::kCUDA, &all_reduce_algo);
-  m.def("plan_algo(int fa, int nbytes, int algo, bool registered) -> int", &plan_algo);
-  m.def("plan(int fa, int nbytes, int algo, bool registered) -> int[]", &plan);
+  m.def("plan_algo(int fa, int nbytes, int algo, bool registered, int dtype=2) -> int", &plan_algo);
+  m.def("plan(int fa, int nbytes, int algo, bool registered, int dtype=2) -> int[]", &plan);
+  m.def("set_auto_table(int fa, int dtype, int[] limits, int[] algos, int fallback) -> ()", &set_auto_table);
+  m.def("get_auto_table(int fa, int dtype) -> (int[], int[], int)", &get_auto_table);
+  m.def("builtin_auto_table(int ws, bool has_nvls) -> (int[], int[], int)", &builtin_auto_table);
+  m.def("choose_auto(int ws, int nbytes, bool has_nvls, bool has_groups, int[] limits, int[] algos, int fallback) "
+        "-> int", &choose_auto);
+  m.def("set_hybrid(int fa, int permille, int p2p_ctas, int nvls_ctas) -> ()", &set_hybrid);
+  m.def("kernel_error_state() -> int[]", &kernel_error_state);
+  m.def("debug_bounds_build() -> bool", &debug_bounds_build);
+#if NAB_DEBUG_BOUNDS
+  m.def("debug_emulate_bad_rank(int[] fas, Tensor[] ins, Tensor(a!)[] outs, int algo) -> ()");
+  m.impl("debug_emulate_bad_rank", c10::kCUDA, &debug_emulate_bad_rank);
+#endif
+  m.def("kernel_error_code() -> int", &kernel_error_code);
+  m.def("kernel_error_reset() -> ()", &kernel_error_reset);
   m.def("emulate_all_reduce(int[] fas, Tensor[] ins, Tensor(a!)[] outs, int algo, int participants=-1) -> ()");
   m.impl("emulate_all_reduce", c10::kCUDA, &emulate_all_reduce);
   m.def("get_graph_buffer_ipc_meta(int fa) -> (int[], int[])", &get_graph_buffer_ipc_meta);

@@ -34,6 +34,7 @@ import torch.distributed as dist
 import torch.nn.functional as F
 
 from ..ops import _ext
+from ..ops.errors import check_enabled, check_kernels
 from ..ops.fused import fused_allreduce_rmsnorm, rmsnorm_residual
 from ..ops.gemm import gemm, gemm_allreduce_rmsnorm, gemm_swiglu, interleave_gate_up, pack_weight
 
@@ -233,6 +234,10 @@ class LlamaTPDecoder:
             self.next_tokens.copy_(allv[best, torch.arange(self.B, device=self.device), 1].long())
         else:
             self.next_tokens.copy_(idx)
+        if check_enabled() and not torch.cuda.is_current_stream_capturing():
+            check_kernels()
+            if self.comm is not None:
+                self.comm.check()
         return self.next_tokens
 
     def reset_position(self):

@@ -28,6 +28,10 @@ CSRC = PKG_DIR / "csrc"
 BUILD_DIR = PKG_DIR / "_build"
 TORCH_LIB = PKG_DIR / "_C.so"
 PLAIN_LIB = PKG_DIR / "libnab.so"
+# Debug variant: the same sources with the device bounds checks compiled in
+# (-DNAB_DEBUG_BOUNDS=1); loaded instead of _C.so when NAB_DEBUG_BUILD=1.
+DEBUG_TORCH_LIB = PKG_DIR / "_C_debug.so"
+DEBUG_DEFINES = ["-DNAB_DEBUG_BOUNDS=1"]
 
 CORE_SOURCES = [
     "nab_allreduce.cu",
@@ -35,6 +39,7 @@ CORE_SOURCES = [
     "nab_gemm_sm100.cu",
     "nab_llama.cu",
     "nab_comm.cpp",
+    "nab_kerr.cpp",
     "nab_nvls.cpp",
     "nab_capi.cpp",
 ]
@@ -139,33 +144,61 @@ def ptxas_report(source: str = "nab_allreduce.cu") -> str:
     return res.stdout + res.stderr
 
 
-def build(verbose: bool = False, jobs: int | None = None) -> dict[str, str]:
-    """Compiles and links both libraries; returns their paths."""
+def build(verbose: bool = False, jobs: int | None = None, debug: bool = False) -> dict[str, str]:
+    """Compiles and links both libraries; returns their paths. ``debug``
+    builds only the torch library, with the device bounds checks, as
+    ``_C_debug.so``."""
     BUILD_DIR.mkdir(exist_ok=True)
     incs, defs, torch_lib = _torch_flags()
+    if debug:
+        defs = defs + DEBUG_DEFINES
     hdr = _headers_digest()
     cuda = cuda_home()
     jobs = jobs or min(8, os.cpu_count() or 2)
+    plain_sources = [] if debug else PLAIN_ONLY_SOURCES
     with cf.ThreadPoolExecutor(max_workers=jobs) as ex:
         core_f = [ex.submit(_compile_one, CSRC / s, False, incs, defs, hdr, verbose) for s in CORE_SOURCES]
         torch_f = [ex.submit(_compile_one, CSRC / s, True, incs, defs, hdr, verbose) for s in TORCH_SOURCES]
-        plain_f = [ex.submit(_compile_one, CSRC / s, False, incs, defs, hdr, verbose) for s in PLAIN_ONLY_SOURCES]
+        plain_f = [ex.submit(_compile_one, CSRC / s, False, incs, defs, hdr, verbose) for s in plain_sources]
         core = [f.result() for f in core_f]
         tobj = [f.result() for f in torch_f]
         pobj = [f.result() for f in plain_f]
     cuda_lib = str(cuda / "lib64")
-    _link(TORCH_LIB, core + tobj,
+    torch_out = DEBUG_TORCH_LIB if debug else TORCH_LIB
+    _link(torch_out, core + tobj,
           [f"-L{torch_lib}", "-lc10", "-ltorch", "-ltorch_cpu", "-lc10_cuda", "-ltorch_cuda",
            f"-L{cuda_lib}", "-lcudart", f"-Wl,-rpath,{torch_lib}"], verbose)
+    if debug:
+        return {"torch": str(torch_out)}
     _link(PLAIN_LIB, core + pobj,
           [f"-L{cuda_lib}", "-lcudart_static", "-ldl", "-lrt", "-lpthread"], verbose)
-    # drop objects that no longer correspond to any current source
+    # drop objects that no longer correspond to any current source (either variant)
     live = {o.name for o in core + tobj + pobj}
+    dbg = {o.name for o in _objects(debug=True)} if DEBUG_TORCH_LIB.exists() else set()
     for o in BUILD_DIR.glob("*.o"):
-        if o.name not in live:
+        if o.name not in live and o.name not in dbg:
             o.unlink()
     return {"torch": str(TORCH_LIB), "plain": str(PLAIN_LIB)}
 
 
+def _objects(debug: bool) -> list[Path]:
+    """Object paths the given variant's current sources map to (no compiling)."""
+    incs, defs, _ = _torch_flags()
+    if debug:
+        defs = defs + DEBUG_DEFINES
+    hdr = _headers_digest()
+    out = []
+    for names, torch_src in ((CORE_SOURCES, False), (TORCH_SOURCES, True)):
+        for n in names:
+            src = CSRC / n
+            key = hashlib.sha256()
+            key.update(src.read_bytes())
+            key.update(hdr.encode())
+            key.update(" ".join(_compile_cmd(src, Path("X"), torch_src, incs, defs)).replace(str(PKG_DIR), "<pkg>")
+                       .encode())
+            out.append(BUILD_DIR / f"{src.stem}-{key.hexdigest()[:16]}.o")
+    return out
+
+
 if __name__ == "__main__":
-    print(build(verbose="-v" in sys.argv))
+    print(build(verbose="-v" in sys.argv, debug="--debug" in sys.argv))

@@ -5,6 +5,8 @@ build is incremental, so calling it on every first import costs only a few
 file hashes when nothing changed. On a machine with a GPU a missing or broken
 library is an error: there is no silent PyTorch fallback for the kernels.
 Set ``NAB_NO_BUILD=1`` to skip the build step and use whatever is on disk.
+``NAB_DEBUG_BUILD=1`` loads ``_C_debug.so`` instead: the same library with the
+device-side bounds checks compiled in (slower; for tests and debugging).
 """
 
 from __future__ import annotations
@@ -19,8 +21,13 @@ _LOCK = threading.Lock()
 _LOADED: str | None = None
 
 
+def _debug() -> bool:
+    return os.environ.get("NAB_DEBUG_BUILD", "0") == "1"
+
+
 def library_path() -> Path:
-    return Path(__file__).resolve().parent.parent / "_C.so"
+    name = "_C_debug.so" if _debug() else "_C.so"
+    return Path(__file__).resolve().parent.parent / name
 
 
 def plain_library_path() -> Path:
@@ -39,7 +46,7 @@ def load():
         if os.environ.get("NAB_NO_BUILD", "0") != "1":
             from .. import native_build
 
-            native_build.build()
+            native_build.build(debug=_debug())
         if not path.exists():
             raise RuntimeError(
                 f"native library {path} is missing; run `python -m numa_allreduce_b200.native_build`")

@@ -10,6 +10,7 @@ from __future__ import annotations
 import torch
 
 from . import _ext
+from .errors import after_launch
 
 TILE_N, TILE_K = 128, 64
 
@@ -69,6 +70,7 @@ def gemm(x: torch.Tensor, wt, out: torch.Tensor | None = None, splits: int | Non
     if out is None:
         out = torch.empty(x.shape[0], N, dtype=torch.bfloat16, device=x.device)
     ops.gemm(x, data, out, int(splits or 0), packed, False)
+    after_launch()
     return out
 
 
@@ -83,6 +85,7 @@ def gemm_swiglu(x: torch.Tensor, wgu, out: torch.Tensor | None = None, splits: i
     if out is None:
         out = torch.empty(x.shape[0], N // 2, dtype=torch.bfloat16, device=x.device)
     ops.gemm(x, data, out, int(splits or 0), packed, True)
+    after_launch()
     return out
 
 
@@ -99,4 +102,7 @@ def gemm_allreduce_rmsnorm(comm, x: torch.Tensor, wt: torch.Tensor, residual: to
         out = torch.empty_like(residual)
     data, _, packed = _operand(wt)
     comm._ops.gemm_ar_rmsnorm(comm._ptr, x, data, residual, weight, out, float(eps), int(splits), packed)
+    if comm.env.check and not torch.cuda.is_current_stream_capturing():
+        torch.cuda.current_stream().synchronize()
+        comm.check()
     return out

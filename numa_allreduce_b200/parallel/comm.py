@@ -43,7 +43,8 @@ from .select import AlgoSelector
 logger = get_logger(__name__)
 
 STAGES = {1: "oneshot", 2: "reduce-scatter", 3: "all-gather", 4: "hier stage 2", 5: "pull start",
-          6: "pull end", 7: "nvls arrive 1", 8: "nvls arrive 2", 9: "fused", 10: "gemm-allreduce"}
+          6: "pull end", 7: "nvls arrive 1", 8: "nvls arrive 2", 9: "fused", 10: "gemm-allreduce",
+          13: "bounds check"}
 
 
 class AllReduceError(RuntimeError):
@@ -74,6 +75,9 @@ class NumaAwareAllReduce:
             protocols are used (no NVLS, no hierarchical groups).
         hier_groups: explicit rank groups for the hierarchical protocol
             (default: NUMA nodes when they split the ranks evenly).
+        hybrid: ``(p2p_permille, p2p_ctas, nvls_ctas)`` split of the hybrid
+            protocol (default: ``NAB_HYBRID``, then the tuning table, then the
+            library's built-in split).
     """
 
     _SUPPORTED_WORLD_SIZES = (1, 2, 3, 4, 5, 6, 7, 8)
@@ -85,7 +89,7 @@ class NumaAwareAllReduce:
                  pipe_tile: int | None = None,
                  hier_groups: list[list[int]] | None = None, topology: NumaTopology | None = None,
                  use_nvls: bool | None = None, timeout_ns: int | None = None,
-                 tuning_file: str | None = None):
+                 tuning_file: str | None = None, hybrid: tuple[int, int, int] | None = None):
         self._IS_CAPTURING = False
         self.disabled = True
         self._ptr = 0
@@ -167,6 +171,12 @@ class NumaAwareAllReduce:
             self.world_size, has_nvls=self._nvls != 0,
             has_groups=bool(self.hier_groups) and self.enable_optimization,
             path=tuning_file or self.env.tuning_file, forced=forced)
+        # the native automatic choice (C ABI, algo=auto) follows the same steps
+        for dt_id, dt_name in ((0, "float32"), (1, "float16"), (2, "bfloat16")):
+            ops.set_auto_table(self._ptr, dt_id, *self.selector.native_table(dt_name))
+        split = hybrid or self.env.hybrid or self.selector.hybrid
+        if split is not None:
+            self.set_hybrid(*split)
         cap = self.env.max_size if self.env.max_size is not None else max_size
         self.max_size = int(cap) if cap is not None else 1 << 62
         self.disabled = False
@@ -327,6 +337,12 @@ class NumaAwareAllReduce:
     @property
     def has_nvls(self) -> bool:
         return self._nvls != 0
+
+    def set_hybrid(self, p2p_permille: int, p2p_ctas: int, nvls_ctas: int) -> None:
+        """Sets the hybrid protocol's split: the share of each message (per
+        mille) that takes the P2P two-shot and the CTAs of each part. Must be
+        the same on every rank."""
+        self._ops.set_hybrid(self._ptr, int(p2p_permille), int(p2p_ctas), int(nvls_ctas))
 
     def algo_for(self, nbytes: int, dtype: torch.dtype = torch.bfloat16, registered: bool = False) -> str:
         """Protocol the selector picks for a message (``"nccl"`` = fall back)."""

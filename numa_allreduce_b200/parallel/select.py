@@ -13,8 +13,19 @@ File format::
 
     {"version": 1,
      "entries": [{"world_size": 8, "dtype": "bfloat16", "nvls": true,
-                  "steps": [[262144, "oneshot"], [17179869184, "nvls_twoshot"]],
-                  "fallback": "nccl"}]}
+                  "steps": [[262144, "oneshot"], [17179869184, "hybrid"]],
+                  "fallback": "nccl"}],
+     "hybrid": {"8": [350, 56, 88]}}
+
+``hybrid`` (optional) gives, per world size, the hybrid protocol's split:
+the P2P share of the message in per mille and the CTAs of its P2P and NVLS
+parts.
+
+The same steps drive the native communicator's automatic choice (the C ABI's
+``numa_all_reduce_*`` calls): :class:`NumaAwareAllReduce` hands the entry of
+each dtype to it, and without a table both sides use the built-in steps that
+the native library defines (``builtin_auto_table``), so the Python path and
+the C path pick the same protocol for every message.
 """
 
 from __future__ import annotations
@@ -23,10 +34,19 @@ import json
 from dataclasses import dataclass, field
 from pathlib import Path
 
-from ..utils.env import ALGO_IDS, NCCL
+from ..ops import _ext
+from ..utils.env import ALGO_IDS, ALGO_NAMES, NCCL, NCCL_ID
 
 DEFAULT_TABLE_PATH = Path(__file__).with_name("tuning_b200.json")
 _BIG = 1 << 62
+
+
+def _algo_id(name: str) -> int:
+    return NCCL_ID if name == NCCL else ALGO_IDS[name]
+
+
+def _algo_name(algo_id: int) -> str:
+    return NCCL if int(algo_id) == NCCL_ID else ALGO_NAMES[int(algo_id)]
 
 
 @dataclass
@@ -45,22 +65,40 @@ class AlgoSelector:
     has_groups: bool = False
     entries: list[Entry] = field(default_factory=list)
     forced: str | None = None
+    hybrid: tuple[int, int, int] | None = None  # measured split of the hybrid protocol
 
     @staticmethod
-    def builtin_steps(world_size: int, has_nvls: bool) -> list[tuple[int, str]]:
-        """Defaults used when no measured table covers a configuration: the
-        push one-shot up to 512 KiB, the pipelined store-based two-shot above
-        (measured fastest on 2 and 8 B200s; NVLS two-shot trailed it)."""
-        return [(512 << 10, "oneshot"), (_BIG, "twoshot_pipe")]
+    def builtin_steps(world_size: int, has_nvls: bool) -> tuple[list[tuple[int, str]], str]:
+        """Steps used when no measured table covers a configuration, as the
+        native library defines them (one definition for both paths)."""
+        limits, algos, fallback = _ext.load().builtin_auto_table(world_size, has_nvls)
+        return [(int(b), ALGO_NAMES[int(a)]) for b, a in zip(limits, algos)], _algo_name(fallback)
 
     @classmethod
     def load(cls, world_size: int, has_nvls: bool, has_groups: bool, path: str | None = None,
              forced: str | None = None) -> "AlgoSelector":
         entries: list[Entry] = []
+        hybrid = None
         p = Path(path) if path else DEFAULT_TABLE_PATH
         if p.exists():
-            entries = parse_table(json.loads(p.read_text()))
-        return cls(world_size, has_nvls, has_groups, entries, forced)
+            obj = json.loads(p.read_text())
+            entries = parse_table(obj)
+            h = obj.get("hybrid", {}).get(str(world_size))
+            if h is not None:
+                hybrid = tuple(int(v) for v in h)
+        return cls(world_size, has_nvls, has_groups, entries, forced, hybrid)
+
+    def steps_for(self, dtype: str) -> tuple[list[tuple[int, str]], str]:
+        """The (steps, fallback) this selector uses for a dtype."""
+        e = self._entry(dtype)
+        if e is not None:
+            return e.steps, e.fallback
+        return self.builtin_steps(self.world_size, self.has_nvls)
+
+    def native_table(self, dtype: str) -> tuple[list[int], list[int], int]:
+        """The steps of a dtype as the native communicator takes them."""
+        steps, fallback = self.steps_for(dtype)
+        return [int(b) for b, _ in steps], [_algo_id(a) for _, a in steps], _algo_id(fallback)
 
     def _entry(self, dtype: str) -> Entry | None:
         best = None
@@ -80,21 +118,26 @@ class AlgoSelector:
             return "copy"
         if self.forced and self.forced != "auto":
             return self._validate(self.forced)
-        e = self._entry(dtype)
-        steps = e.steps if e else self.builtin_steps(self.world_size, self.has_nvls)
-        fallback = e.fallback if e else NCCL
+        steps, fallback = self.steps_for(dtype)
         for limit, algo in steps:
             if nbytes <= limit:
                 return self._validate(algo)
-        return fallback
+        return self._validate(fallback)
 
     def _validate(self, algo: str) -> str:
+        """Substitutes what this group cannot run (same rules as the native
+        ``choose_auto``)."""
         if algo == NCCL:
             return algo
         if algo not in ALGO_IDS:
             raise ValueError(f"unknown protocol {algo!r}")
-        if algo.startswith("nvls") and not self.has_nvls:
-            return "twoshot" if algo == "nvls_twoshot" else "oneshot"
+        if not self.has_nvls:
+            if algo == "nvls_twoshot":
+                return "twoshot"
+            if algo == "nvls_oneshot":
+                return "oneshot"
+            if algo == "hybrid":
+                return "twoshot_pipe"
         if algo == "hier" and not self.has_groups:
             return "twoshot"
         return algo
@@ -113,10 +156,11 @@ def parse_table(obj: dict) -> list[Entry]:
     return out
 
 
-def build_table(results: list[dict], nccl_key: str = NCCL) -> dict:
+def build_table(results: list[dict], nccl_key: str = NCCL, hybrid: dict | None = None) -> dict:
     """Builds a table from sweep rows ``{"world_size", "dtype", "nvls", "bytes",
     "algo", "busbw_gbs"}``: for each size the fastest protocol wins; adjacent
-    sizes with the same winner merge into one step."""
+    sizes with the same winner merge into one step. ``hybrid`` maps a world
+    size to the measured split of the hybrid protocol."""
     groups: dict[tuple, dict[int, dict[str, float]]] = {}
     for r in results:
         k = (int(r["world_size"]), str(r["dtype"]), bool(r.get("nvls", False)))
@@ -135,4 +179,7 @@ def build_table(results: list[dict], nccl_key: str = NCCL) -> dict:
             steps[-1][0] = _BIG  # the custom path wins at the largest size measured: keep it
             fallback = steps[-1][1]
         entries.append({"world_size": ws, "dtype": dtype, "nvls": nvls, "steps": steps, "fallback": fallback})
-    return {"version": 1, "entries": entries}
+    out = {"version": 1, "entries": entries}
+    if hybrid:
+        out["hybrid"] = {str(k): list(v) for k, v in hybrid.items()}
+    return out

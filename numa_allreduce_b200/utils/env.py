@@ -8,8 +8,9 @@ reads. Every variable below is actually read:
 =========================  ===================================================
 ``NAB_DISABLE``            ``1`` disables the custom path (callers fall back)
 ``NAB_ALGO``               force one protocol: ``oneshot``, ``twoshot``,
-                           ``twoshot_pipe``, ``nvls_oneshot``, ``nvls_twoshot``, ``hier``,
-                           ``pull``, ``nccl`` or ``auto`` (default)
+                           ``twoshot_pipe``, ``nvls_oneshot``, ``nvls_twoshot``,
+                           ``hybrid``, ``hier``, ``pull``, ``nccl`` or ``auto``
+                           (default)
 ``NAB_MAX_SIZE``           largest message (bytes) the custom path takes
 ``NAB_TIMEOUT_NS``         bound of every device-side wait (default 5 s)
 ``NAB_TUNING_FILE``        JSON table of protocol thresholds (see select.py)
@@ -21,6 +22,8 @@ reads. Every variable below is actually read:
 ``NAB_NVTX``               ``1`` wraps calls in NVTX ranges
 ``NAB_PIPE_CTAS``          CTAs of the pipelined two-shot (default 128)
 ``NAB_PIPE_TILE``          bytes per ring slot of the pipelined two-shot
+``NAB_HYBRID``             hybrid split ``permille,p2p_ctas,nvls_ctas``: the
+                           P2P share of the message and each part's CTAs
 ``NAB_GEMM_PDL``           ``0`` launches the GEMMs without programmatic
                            dependent launch (read by the native code)
 ``NAB_NO_BUILD``           ``1``: never compile the extension on import
@@ -42,9 +45,11 @@ ALGO_IDS = {
     "pull": 6,
     "copy": 7,
     "twoshot_pipe": 8,
+    "hybrid": 9,
 }
 ALGO_NAMES = {v: k for k, v in ALGO_IDS.items()}
 NCCL = "nccl"
+NCCL_ID = 100  # selector result "use NCCL" (kAlgoNccl in the native library)
 
 
 def _flag(name: str, default: bool = False) -> bool:
@@ -86,6 +91,7 @@ class EnvConfig:
     nvtx: bool = False
     pipe_ctas: int = 128
     pipe_tile: int = 256 << 10
+    hybrid: tuple[int, int, int] | None = None
     extra: dict = field(default_factory=dict)
 
 
@@ -108,4 +114,15 @@ def read_env() -> EnvConfig:
         nvtx=_flag("NAB_NVTX"),
         pipe_ctas=_int("NAB_PIPE_CTAS", 128),
         pipe_tile=_int("NAB_PIPE_TILE", 256 << 10),
+        hybrid=_triple("NAB_HYBRID"),
     )
+
+
+def _triple(name: str) -> tuple[int, int, int] | None:
+    v = os.environ.get(name)
+    if v is None or v.strip() == "":
+        return None
+    parts = [int(x, 0) for x in v.split(",")]
+    if len(parts) != 3:
+        raise ValueError(f"{name} must be 'permille,p2p_ctas,nvls_ctas', got {v!r}")
+    return parts[0], parts[1], parts[2]

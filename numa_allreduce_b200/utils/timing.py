@@ -60,7 +60,7 @@ _NVML_REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown":
 
 def _summarise(rows: list[tuple[float, float, float, set]]) -> dict:
     if not rows:
-        return {"available": False}
+        return {"available": False, "samples": 0}
     reasons = set()
     for r in rows:
         reasons |= r[3]
@@ -75,13 +75,19 @@ pynvml.nvmlInit()
 hs = [pynvml.nvmlDeviceGetHandleByPciBusId(b) for b in ids] if ids else \
      [pynvml.nvmlDeviceGetHandleByIndex(i) for i in range(pynvml.nvmlDeviceGetCount())]
 get = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+mx = [pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM) for h in hs]
+pw = [0.0] * len(hs)
 with open(out, "w", buffering=1) as f:
     print("ready", file=f)
+    k = 0
     while True:
-        for h in hs:
-            f.write("%d,%d,%.1f,%d\n" % (pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
-                    pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM),
-                    pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0, int(get(h))))
+        # SM clock and event reasons every pass; power every 8th pass (slower call)
+        for i, h in enumerate(hs):
+            if k % 8 == 0:
+                pw[i] = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+            f.write("%.6f,%d,%d,%.1f,%d\n" % (time.time(), pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
+                    mx[i], pw[i], int(get(h))))
+        k += 1
         time.sleep(interval)
 """
 
@@ -89,14 +95,17 @@ with open(out, "w", buffering=1) as f:
 class ClockSampler:
     """Samples SM clocks, power and throttle reasons while active.
 
-    Runs in a separate process (NVML, every ``interval_ms``; ``nvidia-smi``
-    if NVML is missing), so the sampling never competes with the benchmark's
-    own kernel launches. ``stop()`` returns ``{"sm_mhz": median,
-    "sm_max_mhz", "power_w_max", "reasons": [...], "samples"}`` over the GPUs
-    whose PCI bus ids were given. It only reads; nothing on the GPU changes.
+    Runs in a separate process (NVML, a pass over the GPUs every
+    ``interval_ms``; ``nvidia-smi`` if NVML is missing), so the sampling never
+    competes with the benchmark's own kernel launches. ``stop(t0, t1)``
+    returns ``{"sm_mhz": median, "sm_max_mhz", "power_w_max", "reasons":
+    [...], "samples"}`` over the GPUs whose PCI bus ids were given, counting
+    only the samples taken between the host times ``t0`` and ``t1``
+    (``time.time()``; the whole run when omitted). It only reads; nothing on
+    the GPU changes.
     """
 
-    def __init__(self, bus_ids: list[str] | None = None, interval_ms: int = 10):
+    def __init__(self, bus_ids: list[str] | None = None, interval_ms: float = 1.0):
         self.bus_ids = list(bus_ids) if bus_ids else []
         self.interval_ms = interval_ms
         self.proc = None
@@ -138,9 +147,9 @@ class ClockSampler:
             time.sleep(0.01)
         return self
 
-    def stop(self) -> dict:
+    def stop(self, t0: float | None = None, t1: float | None = None) -> dict:
         if self.proc is None:
-            return {"available": False}
+            return {"available": False, "samples": 0}
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -156,10 +165,13 @@ class ClockSampler:
         if self.kind == "nvml":
             for line in lines:
                 parts = line.split(",")
-                if len(parts) != 4:
+                if len(parts) != 5:
                     continue
-                bits = int(parts[3])
-                rows.append((float(parts[0]), float(parts[1]), float(parts[2]),
+                ts = float(parts[0])
+                if (t0 is not None and ts < t0) or (t1 is not None and ts > t1):
+                    continue
+                bits = int(parts[4])
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]),
                              {k for k, b in _NVML_REASONS.items() if bits & b}))
         else:
             want = {b.upper().lstrip("0") for b in self.bus_ids}
@@ -178,10 +190,15 @@ class ClockSampler:
         return out
 
 
-def clocks_ok(clocks: dict) -> bool:
-    """False for a run that saw hardware/thermal slowdown or a clock stuck low."""
-    if not clocks.get("available", True):
-        return True
+def clocks_ok(clocks: dict | None, min_samples: int = 10) -> bool | None:
+    """False for a run that saw hardware/thermal slowdown or SM clocks well
+    below the maximum with no reason given (a leftover clock lock); None
+    ("unknown") when fewer than ``min_samples`` samples cover the run."""
+    if not clocks or not clocks.get("available", True) or clocks.get("samples", 0) < min_samples:
+        return None
     if any(r in clocks.get("reasons", []) for r in REJECT_REASONS):
+        return False
+    mhz, top = clocks.get("sm_mhz"), clocks.get("sm_max_mhz")
+    if mhz and top and mhz < 0.8 * top and not clocks.get("reasons"):
         return False
     return True

@@ -77,16 +77,19 @@ def _worker_dead_peer(rank, world, port, mode, result_q):
     from numa_allreduce_b200.parallel.emulate import emulate_allreduce
     from numa_allreduce_b200.parallel.schedule import HierSchedule
 
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=3))
+    # the rendezvous may wait for slow interpreter start-up (a long bound);
+    # only the collectives under test run on a group with a short timeout
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
+    group = dist.new_group(backend="gloo", timeout=timedelta(seconds=3))
     store = dist.distributed_c10d._get_default_store()
     mon = PeerMonitor(store, rank, world, interval_s=0.1, timeout_s=1.0).start()
     sched = HierSchedule.from_groups([[0, 1], [2, 3]] if world == 4 else [list(range(world))])
     x = torch.full((1024,), float(rank + 1))
     # one good step on every rank
-    out = emulate_allreduce(x, sched)
+    out = emulate_allreduce(x, sched, group)
     assert torch.all(out == sum(range(1, world + 1)))
     assert mon.status() == ([], [])  # checked every step
-    dist.barrier()
+    dist.barrier(group=group)
     if rank == world - 1:
         if mode == "raise":
             mon.stop()
@@ -97,7 +100,7 @@ def _worker_dead_peer(rank, world, port, mode, result_q):
     t0 = time.monotonic()
     err = None
     try:
-        emulate_allreduce(x, sched)
+        emulate_allreduce(x, sched, group)
     except Exception as e:  # gloo reports the lost peer or the timeout
         err = type(e).__name__
     waited = time.monotonic() - t0

@@ -94,3 +94,27 @@ def test_gemm_swiglu_epilogue(T, I, K, splits, packed):
     ref = torch.nn.functional.silu(h[:, :I]) * h[:, I:]
     torch.cuda.synchronize()
     torch.testing.assert_close(y.float(), ref, rtol=2e-2, atol=2e-2)
+
+
+def test_kernel_error_record_clean_after_good_launches():
+    """GEMM and attention get the device's kernel error record; good
+    launches leave it at zero (the wait path that writes it is exercised on
+    the host in tests/test_kernel_errors_cpu.py)."""
+    from numa_allreduce_b200 import check_kernels, reset_kernels
+    from numa_allreduce_b200.ops import _ext
+
+    reset_kernels()
+    x = _rand((16, 1024), 7, 1.0)
+    wt = _rand((512, 1024), 8, 0.02)
+    gemm(x, wt)
+    gemm_swiglu(x, interleave_gate_up(wt))
+    ops = _ext.load()
+    q = _rand((2, 8, 128), 9, 1.0)
+    k = _rand((2, 1, 64, 128), 10, 1.0)
+    v = _rand((2, 1, 64, 128), 11, 1.0)
+    pos = torch.tensor([40], dtype=torch.int32, device="cuda")
+    out = torch.empty(2, 8, 128, dtype=torch.bfloat16, device="cuda")
+    ops.decode_attention(q, k, v, pos, out, 2)
+    torch.cuda.synchronize()
+    check_kernels()
+    assert list(ops.kernel_error_state()) == [0] * 8

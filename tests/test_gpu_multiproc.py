@@ -52,7 +52,8 @@ def _worker_correctness(rank, ws, port):
     try:
         ar = NumaAwareAllReduce(dist.group.WORLD, device=rank)
         assert not ar.disabled
-        algos = ["oneshot", "twoshot", "twoshot_pipe"] + (["nvls_oneshot", "nvls_twoshot"] if ar.has_nvls else [])
+        algos = ["oneshot", "twoshot", "twoshot_pipe"] + (
+            ["nvls_oneshot", "nvls_twoshot", "hybrid"] if ar.has_nvls else [])
         if ar.hier_groups:
             algos.append("hier")
         for dtype in (torch.float32, torch.float16, torch.bfloat16):
@@ -75,19 +76,42 @@ def _worker_correctness(rank, ws, port):
                              "hier": HierSchedule.from_groups(ar.hier_groups or [list(range(ws))])}
                     ref = reference_allreduce(xs, sched.get(algo, HierSchedule.twoshot(ws)))
                     got = out.cpu()
-                    if algo.startswith("nvls"):
+                    if algo.startswith("nvls") or algo == "hybrid":
                         # the switch adds in its own order: compare to tolerance, and
                         # check that every rank holds the same bits
                         tol = 1e-5 if dtype == torch.float32 else 1e-2
                         if not torch.allclose(got.float(), ref.float(), rtol=tol, atol=tol):
                             errors.append(f"{algo} {dtype} {shape}: max err "
                                           f"{(got.float() - ref.float()).abs().max().item()}")
-                        if algo == "nvls_twoshot":
+                        if algo in ("nvls_twoshot", "hybrid"):
                             peers = _gather_cpu(out)
                             if not all(torch.equal(p, peers[0]) for p in peers):
                                 errors.append(f"{algo} {dtype} {shape}: ranks disagree")
                     elif not torch.equal(got, ref):
                         errors.append(f"{algo} {dtype} {shape} rank {rank}: not bit-exact")
+        # the native automatic choice (C ABI) agrees with the Python selector
+        from numa_allreduce_b200.utils.env import ALGO_NAMES
+        for dt_id, dtype in ((0, torch.float32), (1, torch.float16), (2, torch.bfloat16)):
+            for k in range(12, 31):
+                py = ar.algo_for(1 << k, dtype)
+                nat = ALGO_NAMES[int(ar._ops.plan_algo(ar._ptr, 1 << k, 0, False, dt_id))]
+                if py != "nccl" and py != nat:
+                    errors.append(f"auto choice differs at {1 << k} bytes {dtype}: python {py}, native {nat}")
+        if ar.has_nvls:
+            # hybrid splits at both extremes and in between, on a ragged size
+            torch.manual_seed(11 + rank)
+            z = torch.randn(3 * (1 << 20) + 40, dtype=torch.bfloat16, device="cuda")
+            exact = torch.stack([t.float() for t in _gather_cpu(z)]).sum(0)
+            for split in ((1, 8, 8), (500, 64, 80), (999, 100, 40), (300, 3, 5)):
+                ar.set_hybrid(*split)
+                got = ar.all_reduce(z, algo="hybrid")
+                torch.cuda.synchronize()
+                if not torch.allclose(got.float().cpu(), exact, rtol=1e-2, atol=1e-2):
+                    errors.append(f"hybrid split {split}: max err {(got.float().cpu() - exact).abs().max().item()}")
+                peers = _gather_cpu(got)
+                if not all(torch.equal(q, peers[0]) for q in peers):
+                    errors.append(f"hybrid split {split}: ranks disagree")
+            ar.set_hybrid(*(ar.selector.hybrid or (400, 64, 80)))
         # public API path with the selector, against the fp32 sum (NCCL's own
         # bf16 result rounds more often, so it is not the oracle here)
         torch.manual_seed(7 + rank)
@@ -274,8 +298,8 @@ def _worker_reinit(rank, ws, port):
 
 def _worker_perf(rank, ws, port, result_q):
     """The reference's performance acceptance (tests/test_numa_all_reduce.py:
-    265-308): fp16 at 64 and 256 MiB, the custom path at least 0.8x NCCL's
-    speed. Device time: CUDA events per call, median, max over ranks."""
+    265-308): fp16 at 64, 256 and 1024 MiB, the custom path at least 0.8x
+    NCCL's speed. Device time: CUDA events per call, median, max over ranks."""
     from numa_allreduce_b200 import NumaAwareAllReduce
 
     _init(rank, ws, port)
@@ -302,7 +326,7 @@ def _worker_perf(rank, ws, port, result_q):
             return t.item()
 
         res = {}
-        for mib in (64, 256):
+        for mib in (64, 256, 1024):
             n = (mib << 20) // 2
             x = torch.randn(n, device="cuda").to(torch.float16)
             out = torch.empty_like(x)

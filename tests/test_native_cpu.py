@@ -32,7 +32,8 @@ def test_c_abi_exports():
     assert lib.nab_workspace_bytes(9) == -1
     for name in ("numa_all_reduce_init", "numa_all_reduce_dispose", "numa_all_reduce_register_buffer",
                  "numa_all_reduce_fp16", "numa_all_reduce_fp32", "numa_all_reduce_bf16", "nab_allreduce",
-                 "nab_last_error", "nab_error_code", "nab_reset"):
+                 "nab_last_error", "nab_error_code", "nab_reset", "nab_set_auto_table", "nab_set_hybrid",
+                 "nab_auto_protocol"):
         assert hasattr(lib, name)
     buf = ctypes.create_string_buffer(256)
     assert lib.nab_last_error(buf, 256) > 0  # message of the failed call above

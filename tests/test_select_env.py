@@ -5,16 +5,76 @@ import json
 import pytest
 
 from numa_allreduce_b200.parallel.select import AlgoSelector, build_table, parse_table
-from numa_allreduce_b200.utils.env import parse_groups, read_env
+from numa_allreduce_b200.utils.env import ALGO_IDS, ALGO_NAMES, parse_groups, read_env
 
 
 def test_builtin_defaults():
     s = AlgoSelector(8, has_nvls=True)
     assert s.choose(4096) == "oneshot"
-    assert s.choose(64 << 20) == "twoshot_pipe"
+    assert s.choose(4 << 20) == "twoshot_pipe"
+    assert s.choose(256 << 20) == "hybrid"
     s = AlgoSelector(8, has_nvls=False)
     assert s.choose(64 << 20) == "twoshot_pipe"
+    assert s.choose(256 << 20) == "twoshot_pipe"
     assert AlgoSelector(1).choose(123) == "copy"
+
+
+def _sizes():
+    out = set()
+    for k in range(4, 31):
+        for d in (-16, 0, 16):
+            if (1 << k) + d > 0:
+                out.add((1 << k) + d)
+    return sorted(out)
+
+
+def _tables():
+    """(label, world size, steps source) for the built-in steps and every
+    entry of the shipped tuning table."""
+    from numa_allreduce_b200.parallel.select import DEFAULT_TABLE_PATH
+
+    cases = [("builtin", ws, None) for ws in range(2, 9)]
+    if DEFAULT_TABLE_PATH.exists():
+        for e in parse_table(json.loads(DEFAULT_TABLE_PATH.read_text())):
+            cases.append((f"table ws{e.world_size} {e.dtype} nvls={e.nvls}", e.world_size, e))
+    return cases
+
+
+@pytest.mark.parametrize("label,ws,entry", _tables(), ids=lambda v: v if isinstance(v, str) else None)
+def test_python_and_native_choice_agree(label, ws, entry):
+    """The Python selector and the native planner's automatic choice (used by
+    the C ABI) pick the same protocol for every size, with and without
+    multicast and groups."""
+    from numa_allreduce_b200.ops import _ext
+
+    ops = _ext.load()
+    for has_nvls in (True, False):
+        if entry is not None and entry.nvls and not has_nvls:
+            continue
+        for has_groups in (True, False):
+            s = AlgoSelector(ws, has_nvls=has_nvls, has_groups=has_groups,
+                             entries=[entry] if entry is not None else [])
+            dtype = entry.dtype if entry is not None else "bfloat16"
+            limits, algos, fallback = s.native_table(dtype)
+            for n in _sizes():
+                py = s.choose(n, dtype)
+                nat = ops.choose_auto(ws, n, has_nvls, has_groups, limits, algos, fallback)
+                assert py == ("nccl" if nat == 100 else ALGO_NAMES[nat]), (label, has_nvls, has_groups, n)
+
+
+def test_shipped_table_is_valid():
+    from numa_allreduce_b200.parallel.select import DEFAULT_TABLE_PATH
+
+    if not DEFAULT_TABLE_PATH.exists():
+        pytest.skip("no tuning table shipped")
+    obj = json.loads(DEFAULT_TABLE_PATH.read_text())
+    entries = parse_table(obj)
+    assert {e.world_size for e in entries} >= {8}
+    for e in entries:
+        assert all(a in ALGO_IDS or a == "nccl" for _, a in e.steps)
+    for ws, split in obj.get("hybrid", {}).items():
+        permille, cp, cn = split
+        assert 0 < permille < 1000 and 1 <= cp and 1 <= cn and cp + cn <= 148
 
 
 def test_forced_and_capabilities():
@@ -64,6 +124,12 @@ def test_env(monkeypatch):
     e = read_env()
     assert e.algo == "hier" and e.hier_groups == [[0, 1, 2, 3], [4, 5, 6, 7]]
     assert e.max_size == 4096 and e.nvls is False
+    monkeypatch.setenv("NAB_HYBRID", "350,56,88")
+    assert read_env().hybrid == (350, 56, 88)
+    monkeypatch.setenv("NAB_HYBRID", "350,56")
+    with pytest.raises(ValueError):
+        read_env()
+    monkeypatch.delenv("NAB_HYBRID")
     monkeypatch.setenv("NAB_ALGO", "nope")
     with pytest.raises(ValueError):
         read_env()

@@ -28,14 +28,20 @@ def test_summary_and_rejection_rules():
     s = _summarise(rows)
     assert s["sm_mhz"] == 1900.0 and s["sm_max_mhz"] == 1965.0 and s["samples"] == 3
     assert s["reasons"] == ["sw_power_cap"]
-    assert clocks_ok(s)  # power capping is kept (and noted)
+    assert clocks_ok(s) is None  # too few samples to vouch for the run
+    s = _summarise(rows * 4)
+    assert clocks_ok(s) is True  # power capping is kept (and noted)
     for bad in ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown"):
-        assert not clocks_ok(dict(s, reasons=[bad]))
-    assert _summarise([]) == {"available": False}
-    assert clocks_ok({"available": False})
+        assert clocks_ok(dict(s, reasons=[bad])) is False
+    # clocks stuck well below the maximum with no reason: a leftover lock
+    assert clocks_ok(dict(s, sm_mhz=1100.0, reasons=[])) is False
+    assert clocks_ok(dict(s, sm_mhz=1300.0, reasons=["sw_power_cap"])) is True
+    assert _summarise([]) == {"available": False, "samples": 0}
+    assert clocks_ok({"available": False}) is None
+    assert clocks_ok(None) is None
 
 
 def test_sampler_without_a_gpu_returns_a_record():
-    rec = ClockSampler([], interval_ms=10).start(wait_s=2.0).stop()
+    rec = ClockSampler([], interval_ms=10).start(wait_s=2.0).stop(0.0, 1e12)
     assert isinstance(rec, dict)
     assert "available" in rec or "samples" in rec
