@@ -8,9 +8,13 @@ RMSNorm eps 1e-5 with weight ones, T in {1, 16, 128, 512}. Variants:
 
   baseline   cuBLAS GEMM (torch.matmul) + NCCL all_reduce + residual add +
              torch RMSNorm (the unfused stack)
-  fused      this library: tcgen05 GEMM whose epilogue stores partial tiles
-             into every rank over NVLink, then rank-order sum + residual +
-             RMSNorm (two launches)
+  fused      this library: tcgen05 GEMM fused with the allreduce, residual
+             add and RMSNorm (two launches), the epilogue picked by size:
+  fused_oneshot  the GEMM epilogue stores partial tiles into every rank over
+             NVLink, then rank-order sum + residual + RMSNorm of every row
+  fused_rs   the GEMM epilogue stores each token row only into its owner
+             rank, the owner reduces + residual + norm, the new residual
+             rows are gathered (reduce-scatter + all-gather bytes)
   lib_unfused  this library's tcgen05 GEMM + fused allreduce/norm kernel
   cublas_fused_ar  cuBLAS GEMM + this library's fused allreduce/norm kernel
 
@@ -113,6 +117,12 @@ def main():
         def fused(i):
             gemm_allreduce_rmsnorm(ar, x, wps[i % copies], res, norm_w, 1e-5, out=out)
 
+        def fused_oneshot(i):
+            gemm_allreduce_rmsnorm(ar, x, wps[i % copies], res, norm_w, 1e-5, out=out, mode="oneshot")
+
+        def fused_rs(i):
+            gemm_allreduce_rmsnorm(ar, x, wps[i % copies], res, norm_w, 1e-5, out=out, mode="reduce_scatter")
+
         def lib_unfused(i):
             gemm(x, wps[i % copies], out=y)
             fused_allreduce_rmsnorm(ar, y, res, norm_w, 1e-5, out=out)
@@ -125,14 +135,15 @@ def main():
         r0 = res.clone()
         baseline(0)
         ref = out.clone()
+        row = {"T": T, "world_size": world}
+        for name, fn in (("fused", fused), ("fused_oneshot", fused_oneshot), ("fused_rs", fused_rs)):
+            res.copy_(r0)
+            fn(0)
+            torch.cuda.synchronize()
+            row[f"max_abs_diff_{name}_vs_baseline"] = (out.float() - ref.float()).abs().max().item()
         res.copy_(r0)
-        fused(0)
-        torch.cuda.synchronize()
-        err = (out.float() - ref.float()).abs().max().item()
-        res.copy_(r0)
-        row = {"T": T, "world_size": world, "max_abs_diff_vs_baseline": err}
-        for name, fn in (("baseline", baseline), ("fused", fused), ("lib_unfused", lib_unfused),
-                         ("cublas_fused_ar", cublas_fused_ar)):
+        for name, fn in (("baseline", baseline), ("fused", fused), ("fused_oneshot", fused_oneshot),
+                         ("fused_rs", fused_rs), ("lib_unfused", lib_unfused), ("cublas_fused_ar", cublas_fused_ar)):
             row[name + "_us"] = round(timed_graph(fn, args.graph_calls, args.reps), 2)
             res.copy_(r0)
         row["speedup_fused_vs_baseline"] = round(row["baseline_us"] / row["fused_us"], 3)

@@ -59,8 +59,10 @@ def parse():
     p.add_argument("--hybrid-configs", default=None,
                    help="hybrid splits to time, e.g. 400x64x80,300x56x88 (P2P per mille x P2P CTAs x NVLS CTAs); "
                         "--write-table keeps the one with the best bus bandwidth summed over sizes >= 16 MiB")
+    p.add_argument("--nvlink", action="store_true",
+                   help="read the NVLink traffic counters around each eager timing (bytes per call per direction)")
     p.add_argument("--merge", action="store_true",
-                   help="--write-table replaces only this world size's entries of an existing table")
+                   help="--write-table replaces only the entries it measured in an existing table")
     return p.parse_args()
 
 
@@ -85,24 +87,47 @@ def pick_hybrid(rows):
     return split, out
 
 
+def merge_tables(old: dict, new: dict) -> dict:
+    """``new``'s entries replace ``old``'s of the same (world size, dtype,
+    nvls); a hybrid split in ``new`` replaces the one of its world size."""
+    keys = {(e["world_size"], e["dtype"], e["nvls"]) for e in new.get("entries", [])}
+    entries = [e for e in old.get("entries", []) if (e["world_size"], e["dtype"], e["nvls"]) not in keys]
+    entries += new.get("entries", [])
+    entries.sort(key=lambda e: (e["world_size"], e["dtype"], e["nvls"]))
+    out = {"version": 1, "entries": entries}
+    hyb = dict(old.get("hybrid", {}))
+    hyb.update(new.get("hybrid", {}))
+    if hyb:
+        out["hybrid"] = hyb
+    return out
+
+
 def max_over_ranks(vals):
     t = torch.tensor(vals, dtype=torch.float64, device="cuda")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return t.tolist()
 
 
-def time_eager(fn, iters, warmup):
+def time_eager(fn, iters, warmup, counters=None):
+    """p50 device time per call (us); with ``counters`` also the NVLink
+    bytes per call per direction read around the timed calls."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
     dist.barrier()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+    before = counters.read() if counters else None
     for a, b in ev:
         a.record()
         fn()
         b.record()
     torch.cuda.synchronize()
-    return statistics.median(a.elapsed_time(b) * 1e3 for a, b in ev)
+    link = None
+    if counters:
+        from numa_allreduce_b200.utils.nvlink import delta
+
+        link = delta(before, counters.read(), iters)
+    return statistics.median(a.elapsed_time(b) * 1e3 for a, b in ev), link
 
 
 def time_graph(fn, calls, reps, warmup):
@@ -166,6 +191,15 @@ def main():
             extra.append((f"pipe_{ctas}x{tile_kib}",
                           NumaAwareAllReduce(dist.group.WORLD, device=local, use_nvls=False, pipe_ctas=ctas,
                                              pipe_tile=tile_kib << 10)))
+    counters = None
+    if args.nvlink and rank == 0:
+        try:
+            from numa_allreduce_b200.utils.nvlink import NvlinkCounters
+            from numa_allreduce_b200.utils.timing import pci_bus_id
+
+            counters = NvlinkCounters(pci_bus_id(local))
+        except Exception as e:  # counters are optional
+            print(f"NVLink counters unavailable: {e}", flush=True)
     sizes = [int(v) for v in args.sizes.split(",")]
     if args.algos == "all":
         algos = ["oneshot", "twoshot", "twoshot_pipe"] + (
@@ -184,7 +218,7 @@ def main():
             g = torch.Generator(device="cuda").manual_seed(rank)
             x = torch.randn(n, generator=g, device="cuda", dtype=torch.float32).to(dtype)
             out = torch.empty_like(x)
-            expect = x.float()
+            expect = x.float().clone()  # for fp32, x.float() is x itself
             dist.all_reduce(expect)
             cands = []
             for algo in algos:
@@ -225,8 +259,9 @@ def main():
                 if not ours and args.mode == "graph":
                     modes = []
                 for mode in modes:
+                    link = None
                     if mode == "eager":
-                        us = time_eager(fn, args.iters, args.warmup)
+                        us, link = time_eager(fn, args.iters, args.warmup, counters)
                     else:
                         reps = max(1, args.iters // args.graph_calls)
                         us = time_graph(fn, args.graph_calls, reps, args.warmup)
@@ -234,10 +269,15 @@ def main():
                     row = {"world_size": world, "dtype": NAMES[dtype], "bytes": size, "algo": label,
                            "mode": mode, "p50_us": round(us, 2), "busbw_gbs": round(busbw_gbs(size, us / 1e6, world), 1),
                            "nvls": ar.has_nvls, "correct": bool(flag.item())}
+                    if link is not None:
+                        row["nvlink_per_call"] = {k: None if v is None else [round(v[0]), round(v[1])]
+                                                  for k, v in link.items()}
                     rows.append(row)
                     if rank == 0:
+                        extra_txt = f" nvlink/call {row['nvlink_per_call']}" if "nvlink_per_call" in row else ""
                         print(f"{NAMES[dtype]:>8} {size:>11} {label:>22} {mode:>5} {us:10.2f} us "
-                              f"{row['busbw_gbs']:8.1f} GB/s {'ok' if row['correct'] else 'WRONG'}", flush=True)
+                              f"{row['busbw_gbs']:8.1f} GB/s {'ok' if row['correct'] else 'WRONG'}{extra_txt}",
+                              flush=True)
     if rank == 0:
         if args.out:
             with open(args.out, "w") as f:
@@ -249,14 +289,7 @@ def main():
             split, tab_rows = pick_hybrid(tab_rows)
             table = build_table(tab_rows, hybrid={world: split} if split else None)
             if args.merge and os.path.exists(args.write_table):
-                with open(args.write_table) as f:
-                    old = json.load(f)
-                table["entries"] = [e for e in old.get("entries", []) if e["world_size"] != world] + table["entries"]
-                table["entries"].sort(key=lambda e: (e["world_size"], e["dtype"], e["nvls"]))
-                hyb = {k: v for k, v in old.get("hybrid", {}).items() if k != str(world)}
-                hyb.update(table.get("hybrid", {}))
-                if hyb:
-                    table["hybrid"] = hyb
+                table = merge_tables(json.load(open(args.write_table)), table)
             with open(args.write_table, "w") as f:
                 json.dump(table, f, indent=1)
     torch.cuda.synchronize()

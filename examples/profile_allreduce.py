@@ -48,26 +48,60 @@ def parse():
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--single", action="store_true", help="emulate --ranks ranks on one GPU (ncu mode)")
     p.add_argument("--ranks", type=int, default=8)
+    p.add_argument("--op", default="allreduce", choices=["allreduce", "fused"],
+                   help="--single: the allreduce, or the fused allreduce + residual + RMSNorm")
+    p.add_argument("--tokens", type=int, default=16, help="--op fused: rows T of the [T, hidden] message")
+    p.add_argument("--hidden", type=int, default=8192, help="--op fused: hidden size H")
+    p.add_argument("--groups", default=None, help="--single with --algo hier: e.g. 0,1,2,3|4,5,6,7")
     return p.parse_args()
 
 
 def single_gpu(args):
-    """ncu-friendly: one process, one GPU, the ranks emulated by one launch."""
+    """ncu-friendly: one process, one GPU, the ranks emulated by one launch.
+    Device time per call (CUDA events, median) is printed with the call."""
     from numa_allreduce_b200.ops.allreduce import EmulatedGroup
+    from numa_allreduce_b200.utils.env import parse_groups
 
     dt = DTYPES[args.dtype]
-    n = int(args.size_mb * (1 << 20)) // torch.tensor([], dtype=dt).element_size()
-    algo = args.algo or "twoshot"
-    with EmulatedGroup(args.ranks) as grp:
-        ins = [torch.randn(n, device="cuda").to(dt) for _ in range(args.ranks)]
-        outs = [torch.empty_like(x) for x in ins]
-        for _ in range(3 if args.mode == "ncu" else args.iters):
-            grp.all_reduce(ins, algo=algo, outs=outs)
+    algo = args.algo or ("twoshot" if args.op == "allreduce" else "auto")
+    groups = parse_groups(args.groups) if args.groups else None
+    iters = 3 if args.mode == "ncu" else args.iters
+    # the emulation runs at most 148 / ranks CTAs per rank: size the rings for that
+    with EmulatedGroup(args.ranks, groups=groups, pipe_ctas=max(1, 148 // args.ranks),
+                       fused_bytes=max(512 << 10, args.tokens * args.hidden * 2)) as grp:
+        if args.op == "allreduce":
+            n = int(args.size_mb * (1 << 20)) // torch.tensor([], dtype=dt).element_size()
+            ins = [torch.randn(n, device="cuda").to(dt) for _ in range(args.ranks)]
+            outs = [torch.empty_like(x) for x in ins]
+            nbytes = n * ins[0].element_size()
+
+            def call():
+                grp.all_reduce(ins, algo=algo, outs=outs)
+        else:
+            T, H = args.tokens, args.hidden
+            ins = [torch.randn(T, H, device="cuda").to(torch.bfloat16) for _ in range(args.ranks)]
+            res = [torch.randn(T, H, device="cuda").to(torch.bfloat16) for _ in range(args.ranks)]
+            wts = [torch.ones(H, device="cuda", dtype=torch.bfloat16) for _ in range(args.ranks)]
+            outs = [torch.empty_like(x) for x in ins]
+            nbytes = T * H * 2
+
+            def call():
+                grp.fused_ar_rmsnorm(ins, res, wts, eps=1e-5, algo=algo, outs=outs)
+        call()  # first call outside the timing
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(iters):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            call()
+            b.record()
+            times.append((a, b))
         torch.cuda.synchronize()
         if any(grp.error_codes()):
-            raise RuntimeError(f"emulated allreduce reported errors: {grp.error_states()}")
-    print(json.dumps({"mode": args.mode, "single": True, "ranks": args.ranks, "algo": algo,
-                      "bytes": n * ins[0].element_size()}))
+            raise RuntimeError(f"emulated {args.op} reported errors: {grp.error_states()}")
+        us = sorted(a.elapsed_time(b) * 1e3 for a, b in times)[len(times) // 2]
+    print(json.dumps({"mode": args.mode, "single": True, "op": args.op, "ranks": args.ranks, "algo": algo,
+                      "bytes_per_rank": nbytes, "us_per_call": round(us, 2)}))
 
 
 def multi_rank(args):

@@ -67,21 +67,17 @@ CommConfig config_from_list(const std::vector<int64_t>& v) {
 }
 
 AutoTable builtin_auto_table(int ws, bool has_nvls) {
+  (void)has_nvls;
   AutoTable t;
   if (ws <= 1) {
     t.steps = {{int64_t(1) << 62, kAlgoCopy}};
     return t;
   }
-  // push one-shot for latency-bound sizes, the pipelined store two-shot in the
-  // middle, and on NVSwitch systems with multicast the hybrid (P2P + NVLS in
-  // one launch) for large messages
+  // push one-shot for latency-bound sizes, the pipelined store two-shot above
+  // (measured fastest of this library's protocols at 2, 4 and 8 B200s; the
+  // NVLS and hybrid protocols trailed it at every size)
   t.steps.push_back({512 << 10, kAlgoOneshot});
-  if (has_nvls) {
-    t.steps.push_back({int64_t(kHybridMinBytes) - 1, kAlgoTwoshotPipe});
-    t.steps.push_back({int64_t(1) << 62, kAlgoHybrid});
-  } else {
-    t.steps.push_back({int64_t(1) << 62, kAlgoTwoshotPipe});
-  }
+  t.steps.push_back({int64_t(1) << 62, kAlgoTwoshotPipe});
   t.fallback = kAlgoNccl;
   return t;
 }
@@ -116,8 +112,8 @@ Layout make_layout(int ws, const CommConfig& cfg) {
   if (cfg.pipe_tile < (64 << 10) || cfg.pipe_tile > (4 << 20))
     throw std::invalid_argument("pipe_tile must be in [64 KiB, 4 MiB]");
   if (cfg.hybrid_p2p_permille < 0 || cfg.hybrid_p2p_permille > 1000 || cfg.hybrid_p2p_ctas < 1 ||
-      cfg.hybrid_p2p_ctas > cfg.pipe_ctas || cfg.hybrid_nvls_ctas < 1 || cfg.hybrid_nvls_ctas > kNvlsCtas)
-    throw std::invalid_argument("hybrid split: permille in [0, 1000], P2P CTAs <= pipe_ctas, NVLS CTAs <= 128");
+      cfg.hybrid_p2p_ctas > kMaxBlocks || cfg.hybrid_nvls_ctas < 1 || cfg.hybrid_nvls_ctas > kNvlsCtas)
+    throw std::invalid_argument("hybrid split: permille in [0, 1000], P2P CTAs in [1, 160], NVLS CTAs in [1, 128]");
   Layout L{};
   int64_t off = round_up(static_cast<int64_t>(sizeof(SignalPad)), kAlign);
   L.oneshot_off = off;
@@ -196,6 +192,8 @@ const AutoTable& Communicator::auto_table(int dtype) const {
 }
 
 void Communicator::set_hybrid(int p2p_permille, int p2p_ctas, int nvls_ctas) {
+  if (p2p_ctas > cfg_.pipe_ctas)
+    throw std::invalid_argument("hybrid split: more P2P CTAs than the pipelined ring has slots (pipe_ctas)");
   CommConfig c = cfg_;
   c.hybrid_p2p_permille = p2p_permille;
   c.hybrid_p2p_ctas = p2p_ctas;
@@ -370,7 +368,7 @@ LaunchPlan Communicator::plan(int64_t nbytes, int algo, bool registered, int dty
       // the split point is a multiple of 16 packs (256 B) and both parts are
       // non-empty
       const int64_t permille = clampv<int64_t>(cfg_.hybrid_p2p_permille, 1, 999);
-      const int cp_max = cfg_.hybrid_p2p_ctas;
+      const int cp_max = std::min(cfg_.hybrid_p2p_ctas, L_.pipe_ctas);
       const int cn_max = cfg_.hybrid_nvls_ctas;
       const int64_t split = clampv<int64_t>((npacks * permille / 1000) / 16 * 16, 16, (npacks - 1) / 16 * 16);
       const int64_t rest = npacks - split;

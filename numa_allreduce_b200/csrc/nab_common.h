@@ -150,8 +150,6 @@ constexpr int64_t kNvlsTileBytes = 256 << 10;  // one ring slot: ws chunks
 constexpr int kHybridP2pPermille = 400;
 constexpr int kHybridP2pCtas = 64;
 constexpr int kHybridNvlsCtas = 80;
-// Smallest message the built-in steps give to the hybrid protocol.
-constexpr int64_t kHybridMinBytes = int64_t(32) << 20;
 
 constexpr uint64_t kSeqShift = 20;  // rounds per call < 2^20
 

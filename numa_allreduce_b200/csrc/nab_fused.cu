@@ -327,6 +327,122 @@ __global__ void __launch_bounds__(kFThreads) k_slots_rmsnorm(const char* base, i
   }
 }
 
+// Second half of the reduce-scatter GEMM + allreduce. Row t is owned by rank
+// t % ws and its partials from every rank are in the owner's slots. Row
+// blocks k hold rows [k ws, (k + 1) ws); CTA c takes blocks c, c + C, ...
+//   phase A  for the owned row of each block: wait (bounded) for every rank's
+//            tiles covering it, add the ws partials in rank order and the
+//            residual -> z (bf16); residual = z, out = norm(z); z replaces
+//            this rank's own partial of the row in its slot (published);
+//   exchange release this CTA's flag on every peer, acquire every peer's;
+//   phase B  for the other owners' rows of the same blocks: pull z from the
+//            owner's slot, residual = z, out = norm(z).
+// Every rank computes the norm from the same bf16 z, so all hold the same
+// bits. A slot's parity is reused two calls later; by then every peer has
+// passed this call's exchange of the next call, so nobody still reads it.
+struct RsNormArgs {
+  char* wsp[kMaxRanks];
+  int64_t slot_off;
+  int64_t slot_bytes;
+  int ws;
+  int rank;
+  int tile_tokens;
+  int m_tiles;
+  WaitCtx w;
+  uint4* residual;
+  const uint4* wgt;
+  uint4* out;
+  int T;
+  int H;
+  float eps;
+};
+
+template <int PPT>
+__global__ void __launch_bounds__(kFThreads) k_slots_rs_rmsnorm(const __grid_constant__ RsNormArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int rank = a.rank, ws = a.ws;
+  const SignalPad* pad = reinterpret_cast<const SignalPad*>(a.wsp[rank]);
+  const uint32_t epoch = ld_volatile_u32(&pad->epoch);
+  const int parity = epoch & 1;
+  WaitCtx w = a.w;
+  w.epoch = epoch;
+  const int hp = a.H / 8;
+  const int nblocks = (a.T + ws - 1) / ws;
+  auto slot_row = [&](int owner, int src, int t) -> uint4* {
+    return reinterpret_cast<uint4*>(a.wsp[owner] + a.slot_off + (static_cast<int64_t>(parity) * ws + src) * a.slot_bytes) +
+           static_cast<int64_t>(t) * hp;
+  };
+  // ---- phase A: owned rows
+  int ready_tile = -1;
+  bool ok = true;
+  for (int k = blockIdx.x; k < nblocks && ok; k += gridDim.x) {
+    const int t = k * ws + rank;
+    if (t >= a.T) continue;
+    if (t / a.tile_tokens != ready_tile) {
+      ready_tile = t / a.tile_tokens;
+      bool fine = true;
+      for (int i = threadIdx.x; i < a.m_tiles * ws; i += kFThreads) {
+        const int m = i / ws, q = i % ws;
+        fine &= wait_geq(&pad->gemm_flags[ready_tile * a.m_tiles + m][q], make_seq(epoch, 0), w,
+                         static_cast<uint32_t>(q), kStageGemmAR);
+      }
+      ok = __syncthreads_and(fine) != 0;
+      if (!ok) break;
+    }
+    float z[PPT][8];
+    float ss = 0.f;
+    const int64_t o = static_cast<int64_t>(t) * hp;
+#pragma unroll
+    for (int kk = 0; kk < PPT; ++kk) {
+      const int idx = threadIdx.x + kk * kFThreads;
+      if (idx < hp) {
+        uint4 v[kMaxRanks];
+#pragma unroll
+        for (int q = 0; q < kMaxRanks; ++q)
+          if (q < ws) v[q] = ld_cg(slot_row(rank, q, t) + idx);
+        Acc<__nv_bfloat16> acc;
+        acc_set(acc, v[0]);
+#pragma unroll
+        for (int q = 1; q < kMaxRanks; ++q)
+          if (q < ws) acc_add(acc, v[q]);
+        ss += finish_pack(acc, ld_plain(a.residual + o + idx), a.residual + o + idx, slot_row(rank, rank, t) + idx,
+                          z[kk]);
+      }
+    }
+    norm_store<PPT>(z, ss, a.wgt, a.out + o, hp, a.H, a.eps);
+  }
+  // ---- exchange with every peer (the same CTA index), then phase B
+  int peers[kMaxRanks];
+  all_peers_rt(ws, rank, peers);
+  ok = exchange(a.wsp, rank, kFlagFusedAG, blockIdx.x, make_seq(epoch, 1), peers, ok ? ws - 1 : 0, w, kStageAG) &&
+       ok;
+  if (!ok) return;
+  for (int k = blockIdx.x; k < nblocks; k += gridDim.x) {
+    for (int j = 0; j < ws - 1; ++j) {
+      const int q = peers[j];
+      const int t = k * ws + q;
+      if (t >= a.T) continue;
+      const uint4* src = slot_row(q, q, t);
+      const int64_t o = static_cast<int64_t>(t) * hp;
+      float z[PPT][8];
+      float ss = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < PPT; ++kk) {
+        const int idx = threadIdx.x + kk * kFThreads;
+        if (idx < hp) {
+          const uint4 zb = ld_cg(src + idx);
+          st_plain(a.residual + o + idx, zb);
+          unpack_bf16(zb, z[kk]);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) ss += z[kk][e] * z[kk][e];
+        }
+      }
+      norm_store<PPT>(z, ss, a.wgt, a.out + o, hp, a.H, a.eps);
+    }
+  }
+}
+
 template <int WS, int PPT>
 void* pick_kernel(int algo) {
   return algo == kFusedOneshot ? reinterpret_cast<void*>(&k_fused_oneshot<WS, PPT>)
@@ -474,6 +590,49 @@ void slots_rmsnorm(Communicator& c, cudaStream_t s, void* residual, const void* 
   }
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string("slots rmsnorm launch failed: ") + cudaGetErrorString(e));
+  c.count_launch();
+}
+
+void slots_rs_rmsnorm(Communicator& c, cudaStream_t s, void* residual, const void* weight, void* out, int64_t T,
+                      int64_t H, float eps, int tile_tokens) {
+  check_shape(T, H);
+  if (reinterpret_cast<uintptr_t>(residual) % 16 || reinterpret_cast<uintptr_t>(weight) % 16 ||
+      reinterpret_cast<uintptr_t>(out) % 16)
+    throw std::invalid_argument("slots rmsnorm: 16-byte alignment");
+  if (H % 128 != 0 || tile_tokens < 1) throw std::invalid_argument("slots rmsnorm: H must be a multiple of 128");
+  const int ws = c.world_size();
+  const Layout& L = c.layout();
+  RsNormArgs a{};
+  for (int r = 0; r < ws; ++r) a.wsp[r] = c.wsp(r);
+  a.slot_off = L.fused_off;
+  a.slot_bytes = L.fused_bytes;
+  a.ws = ws;
+  a.rank = c.rank();
+  a.tile_tokens = tile_tokens;
+  a.m_tiles = static_cast<int>(H / 128);
+  a.w.err = c.err_dev();
+  a.w.err_host = c.err_host();
+  a.w.abort = &reinterpret_cast<SignalPad*>(c.wsp(c.rank()))->abort;
+  a.w.timeout_ns = c.config().timeout_ns;
+  a.w.rank = static_cast<uint32_t>(c.rank());
+  a.residual = static_cast<uint4*>(residual);
+  a.wgt = static_cast<const uint4*>(weight);
+  a.out = static_cast<uint4*>(out);
+  a.T = static_cast<int>(T);
+  a.H = static_cast<int>(H);
+  a.eps = eps;
+  // one CTA per row block, at most one per flag slot; every CTA of every
+  // rank must be resident at once (they wait on each other): 256 threads,
+  // no dynamic shared memory, far below the device's capacity
+  const int grid = static_cast<int>(std::min<int64_t>((T + ws - 1) / ws, 148));
+  switch (ppt_for(H)) {
+    case 1: launch_pdl(k_slots_rs_rmsnorm<1>, grid, kFThreads, s, a); break;
+    case 2: launch_pdl(k_slots_rs_rmsnorm<2>, grid, kFThreads, s, a); break;
+    case 4: launch_pdl(k_slots_rs_rmsnorm<4>, grid, kFThreads, s, a); break;
+    default: launch_pdl(k_slots_rs_rmsnorm<8>, grid, kFThreads, s, a); break;
+  }
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string("slots rs rmsnorm launch failed: ") + cudaGetErrorString(e));
   c.count_launch();
 }
 

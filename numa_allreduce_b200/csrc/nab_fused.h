@@ -42,6 +42,14 @@ int emulate_fused_allreduce_rmsnorm(const std::vector<Communicator*>& comms, cud
 void slots_rmsnorm(Communicator& c, cudaStream_t s, void* residual, const void* weight, void* out, int64_t T,
                    int64_t H, float eps, int tile_tokens);
 
+// Second half of the reduce-scatter GEMM + allreduce: this rank's slots hold
+// every rank's partial of the rows it owns (t % ws == rank); reduces them in
+// rank order + residual + RMSNorm, publishes the new residual rows in place,
+// exchanges a flag with every peer and pulls the other owners' residual rows
+// (recomputing their norm locally).
+void slots_rs_rmsnorm(Communicator& c, cudaStream_t s, void* residual, const void* weight, void* out, int64_t T,
+                      int64_t H, float eps, int tile_tokens);
+
 // Local residual add + RMSNorm (no communication): the world-size-1 path and
 // the norm of the unfused baseline.
 void rmsnorm_residual(cudaStream_t s, const void* inp, void* residual, const void* weight, void* out,

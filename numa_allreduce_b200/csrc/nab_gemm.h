@@ -32,15 +32,27 @@ int gemm_splits_for(int T, int N, int K, int sms);
 // Clusters of cs CTAs of the bn-token-wide kernel the device runs at once.
 int gemm_active_clusters(int bn, int cs);
 
-// Row-parallel layer tail in two launches: the GEMM whose epilogue stores
-// each finished bf16 output tile into this rank's slot on every rank over
-// NVLink and raises the tile's flag there, then the kernel that waits for
-// each row's tiles and does the rank-order sum + residual add + RMSNorm.
+// Row-parallel layer tail in two launches, in one of two modes:
+//  one-shot        the GEMM's epilogue stores each finished bf16 output tile
+//                  into this rank's slot on every rank over NVLink and raises
+//                  the tile's flag there; the second kernel waits for each
+//                  row's tiles and does the rank-order sum + residual add +
+//                  RMSNorm of every row;
+//  reduce-scatter  the epilogue stores token row t only into its owner rank
+//                  t % ws; the second kernel reduces the owned rows (rank
+//                  order) + residual + RMSNorm, publishes each new residual
+//                  row in place, and every rank pulls the other owners'
+//                  residual rows and recomputes the norm locally:
+//                  2 (ws - 1) / ws of the output crosses NVLink instead of
+//                  (ws - 1) times it.
 // residual is updated in place; out receives the normalised activations.
 // splits as for gemm_bf16 (split partials are added on this GPU, so only
 // bf16 tiles cross NVLink). Returns the split count used.
+enum GemmArMode : int { kGemmArAuto = 0, kGemmArOneshot = 1, kGemmArReduceScatter = 2 };
 int gemm_allreduce_rmsnorm(Communicator& c, cudaStream_t s, const void* wt, const void* x, void* residual,
                            const void* weight, void* out, int T, int N, int K, float eps, int splits,
-                           bool packed = false);
+                           bool packed = false, int mode = kGemmArAuto);
+// The mode kGemmArAuto picks for T tokens on ws ranks.
+int gemm_ar_mode_for(int T, int ws);
 
 }  // namespace nab

@@ -81,6 +81,7 @@ struct GemmArgs {
   int ws;
   int64_t slot_off;    // fused one-shot slots: [2 parities][ws][slot_bytes]
   int64_t slot_bytes;
+  int rs;              // reduce-scatter epilogue: token row t goes only to rank t % ws
   ErrorState* err;
   uint32_t* err_host;
   uint64_t timeout_ns;
@@ -320,6 +321,11 @@ __global__ void __launch_bounds__(kGemmThreads, GemmCfg<BN>::kCtasPerSm)
       const int64_t eoff = static_cast<int64_t>(t0 + t) * ldo + m_tile * out_cols + f;  // element offset
       if (!g.fused) {
         *reinterpret_cast<uint4*>(g.out + eoff) = packed;
+      } else if (g.rs) {
+        // reduce-scatter by stores: only the row's owner gets it
+        const int dst = (t0 + t) % g.ws;
+        char* slot = g.wsp[dst] + g.slot_off + (static_cast<int64_t>(parity) * g.ws + g.rank) * g.slot_bytes;
+        *reinterpret_cast<uint4*>(slot + eoff * 2) = packed;
       } else {
         // into this rank's slot on every rank (its own included), staggered
         for (int k = 0; k < g.ws; ++k) {
@@ -517,6 +523,14 @@ void check_shape(int T, int N, int K) {
 
 int gemm_active_clusters(int bn, int cs) { return active_clusters(bn, cs); }
 
+int gemm_ar_mode_for(int T, int ws) {
+  // One-shot: every rank's whole output crosses to every peer ((ws - 1) T H
+  // elements per direction) but needs no second exchange; reduce-scatter +
+  // gather moves 2 (ws - 1) / ws T H and adds one flag round trip. From a few
+  // rows per rank on, the bytes win.
+  return T >= 8 * ws ? kGemmArReduceScatter : kGemmArOneshot;
+}
+
 int gemm_splits_for(int T, int N, int K, int sms) {
   (void)sms;  // the device's own occupancy answer accounts for the SMs
   const int bn = pick_bn(T);
@@ -565,7 +579,8 @@ void gemm_bf16(cudaStream_t s, const void* wt, const void* x, void* y, int T, in
 }
 
 int gemm_allreduce_rmsnorm(Communicator& c, cudaStream_t s, const void* wt, const void* x, void* residual,
-                           const void* weight, void* out, int T, int N, int K, float eps, int splits, bool packed) {
+                           const void* weight, void* out, int T, int N, int K, float eps, int splits, bool packed,
+                           int mode) {
   check_shape(T, N, K);
   const Layout& L = c.layout();
   if (c.world_size() == 1) throw std::invalid_argument("GEMM+allreduce needs a world size of at least 2");
@@ -590,9 +605,14 @@ int gemm_allreduce_rmsnorm(Communicator& c, cudaStream_t s, const void* wt, cons
   g.err = c.err_dev();
   g.err_host = c.err_host();
   g.timeout_ns = c.config().timeout_ns;
+  if (mode == kGemmArAuto) mode = gemm_ar_mode_for(T, c.world_size());
+  g.rs = mode == kGemmArReduceScatter ? 1 : 0;
   launch(wt, x, g, bn, s);
   c.count_launch();
-  slots_rmsnorm(c, s, residual, weight, out, T, N, eps, bn);
+  if (g.rs)
+    slots_rs_rmsnorm(c, s, residual, weight, out, T, N, eps, bn);
+  else
+    slots_rmsnorm(c, s, residual, weight, out, T, N, eps, bn);
   return g.splits;
 }
 

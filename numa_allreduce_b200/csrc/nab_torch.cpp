@@ -397,7 +397,8 @@ int64_t gemm_splits(int64_t T, int64_t N, int64_t K) {
 }
 
 void gemm_ar_rmsnorm(fptr_t fa, const at::Tensor& x, const at::Tensor& wt, at::Tensor& residual,
-                     const at::Tensor& weight, at::Tensor& out, double eps, int64_t splits, bool packed) {
+                     const at::Tensor& weight, at::Tensor& out, double eps, int64_t splits, bool packed,
+                     int64_t mode) {
   check_gemm_operand(x, "x");
   check_gemm_operand(wt, "wt");
   check_gemm_operand(residual, "residual");
@@ -415,8 +416,10 @@ void gemm_ar_rmsnorm(fptr_t fa, const at::Tensor& x, const at::Tensor& wt, at::T
   auto stream = at::cuda::getCurrentCUDAStream().stream();
   nab::gemm_allreduce_rmsnorm(*C(fa), stream, wt.data_ptr(), x.data_ptr(), residual.data_ptr(), weight.data_ptr(),
                               out.data_ptr(), static_cast<int>(x.size(0)), static_cast<int>(N), static_cast<int>(K),
-                              static_cast<float>(eps), static_cast<int>(splits), packed);
+                              static_cast<float>(eps), static_cast<int>(splits), packed, static_cast<int>(mode));
 }
+
+int64_t gemm_ar_mode(int64_t T, int64_t ws) { return nab::gemm_ar_mode_for(static_cast<int>(T), static_cast<int>(ws)); }
 
 void rope_append_op(const at::Tensor& qkv, const at::Tensor& cos_t, const at::Tensor& sin_t, const at::Tensor& pos,
                     at::Tensor& q_out, at::Tensor& k_cache, at::Tensor& v_cache, int64_t Hq, int64_t Hkv) {
@@ -539,7 +542,8 @@ TORCH_LIBRARY(nab, m) {
   m.def("gemm_splits(int T, int N, int K) -> int", &gemm_splits);
   m.def("gemm_active_clusters(int bn, int cs) -> int", &gemm_active_clusters);
   m.def("gemm_ar_rmsnorm(int fa, Tensor x, Tensor wt, Tensor(a!) residual, Tensor weight, Tensor(b!) out, "
-        "float eps, int splits=0, bool packed=False) -> ()");
+        "float eps, int splits=0, bool packed=False, int mode=0) -> ()");
+  m.def("gemm_ar_mode(int T, int ws) -> int", &gemm_ar_mode);
   m.impl("gemm_ar_rmsnorm", c10::kCUDA, &gemm_ar_rmsnorm);
   m.def("rope_append(Tensor qkv, Tensor cos, Tensor sin, Tensor pos, Tensor(a!) q_out, Tensor(b!) k_cache, "
         "Tensor(c!) v_cache, int Hq, int Hkv) -> ()");

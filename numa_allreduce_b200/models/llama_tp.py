@@ -71,10 +71,12 @@ def _round_up(x: int, a: int) -> int:
 class LlamaTPDecoder:
     """One rank's shard of the model plus the static buffers of a decode step.
 
-    Row-parallel tails with up to ``FUSED_GEMM_MAX_TOKENS`` tokens use the
-    fused GEMM + allreduce; above that (measured on 8 B200s: 75.9 us fused vs
-    67.0 us for cuBLAS + fused allreduce-norm at 512 tokens, Llama-3-8B down
-    projection) a library GEMM feeds the fused allreduce + norm kernel.
+    Row-parallel tails use the fused GEMM + allreduce + norm whenever the
+    output fits the communicator's fused slots (``fused_bytes``): the one-shot
+    epilogue for a few tokens, the reduce-scatter epilogue (each token row to
+    its owner rank, then a gather of the new residual rows) from 8 tokens per
+    rank on. Larger outputs take this library's GEMM followed by its fused
+    allreduce + residual + RMSNorm kernel. No library GEMM is on the path.
 
     Args:
         cfg: model shape.
@@ -88,8 +90,6 @@ class LlamaTPDecoder:
             tensor-parallel model (same per-GPU shapes, no allreduce), to
             study one rank's kernels alone.
     """
-
-    FUSED_GEMM_MAX_TOKENS = 128
 
     def __init__(self, cfg: LlamaConfig, comm, batch: int, context: int, impl: str = "fused", seed: int = 0,
                  device: torch.device | str = "cuda", attn_splits: int | None = None, shard_of: int | None = None):
@@ -194,16 +194,20 @@ class LlamaTPDecoder:
         if self.world == 1:
             gemm(inp, self._w(layer, key), out=self.y)
             rmsnorm_residual(self.y, self.h, norm_w, eps, out=self.x)
-        elif self.B <= self.FUSED_GEMM_MAX_TOKENS and self.B * self.cfg.hidden * 2 <= self.comm.fused_bytes:
+        elif self.B * self.cfg.hidden * 2 <= self.comm.fused_bytes:
+            # one-shot epilogue for few tokens, reduce-scatter epilogue from 8
+            # tokens per rank on (both this library's tcgen05 GEMM)
             gemm_allreduce_rmsnorm(self.comm, inp, self._w(layer, key), self.h, norm_w, eps, out=self.x)
         else:
-            # prefill-sized token counts: a plain library GEMM on the row-major
-            # weight, then this library's fused allreduce + residual + RMSNorm
-            torch.matmul(inp, w_rows.t(), out=self.y)
+            # more rows than the fused slots hold: this library's GEMM, then its
+            # fused allreduce + residual + RMSNorm
+            gemm(inp, self._w(layer, key), out=self.y)
             fused_allreduce_rmsnorm(self.comm, self.y, self.h, norm_w, eps, out=self.x)
 
-    def step(self):
-        """One decode step (graph-capturable): tokens -> next tokens."""
+    def step(self, trace: list | None = None):
+        """One decode step (graph-capturable): tokens -> next tokens. With
+        ``trace`` (eager only) the residual stream after every layer is
+        appended to it as fp32."""
         cfg, ops = self.cfg, self.ops
         torch.index_select(self.embed, 0, self.tokens, out=self.h)
         self.x.copy_(F.rms_norm(self.h, (cfg.hidden,), self.layers[0]["in_norm"], cfg.eps))
@@ -224,6 +228,8 @@ class LlamaTPDecoder:
                 gemm_swiglu(self.x, self._w(i, "wgu"), out=self.act)
             nxt = self.layers[i + 1]["in_norm"] if i + 1 < len(self.layers) else self.final_norm
             self._row_parallel_tail(self.act, i, "wd", nxt)
+            if trace is not None:
+                trace.append(self.h.float().clone())
         self._proj(self.x, self._w(-1, "lm_head"), self.logits)
         val, idx = self.logits.float().max(dim=-1)
         if self.world > 1:
@@ -242,6 +248,51 @@ class LlamaTPDecoder:
 
     def reset_position(self):
         self.pos.fill_(self.ctx)
+
+    @torch.no_grad()
+    def reference_step_fp32(self) -> list[torch.Tensor]:
+        """The same decode step in fp32 PyTorch from the same (bf16) weights
+        and KV cache, on one GPU (world size 1, or a ``shard_of`` shard):
+        returns the residual stream after every layer. Positions before the
+        current one come from the cache; the current position's k and v are
+        this function's own (the cache is not written)."""
+        if self.world != 1:
+            raise ValueError("the fp32 reference runs on one GPU (world size 1 or shard_of)")
+        cfg = self.cfg
+        D, B, Hq, Hkv = cfg.head_dim, self.B, self.Hq, self.Hkv
+        pos = int(self.pos.item())
+        c, s = self.cos[pos], self.sin[pos]
+
+        def rot(t):
+            a, b = t[..., :D // 2], t[..., D // 2:]
+            return torch.cat([a * c - b * s, b * c + a * s], dim=-1)
+
+        def norm(t, w):
+            return t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + cfg.eps) * w.float()
+
+        h = self.embed.index_select(0, self.tokens).float()
+        x = norm(h, self.layers[0]["in_norm"])
+        out = []
+        for i, L in enumerate(self.layers):
+            qkv = x @ L["wqkv"].float().t()
+            q = rot(qkv[:, :Hq * D].view(B, Hq, D))
+            k_new = rot(qkv[:, Hq * D:(Hq + Hkv) * D].view(B, Hkv, D))
+            v_new = qkv[:, (Hq + Hkv) * D:].view(B, Hkv, D)
+            k = torch.cat([L["k"][:, :, :pos].float(), k_new[:, :, None]], dim=2)
+            v = torch.cat([L["v"][:, :, :pos].float(), v_new[:, :, None]], dim=2)
+            g = Hq // Hkv
+            k, v = k.repeat_interleave(g, dim=1), v.repeat_interleave(g, dim=1)
+            p = (torch.einsum("bhd,bhld->bhl", q, k) / math.sqrt(D)).softmax(-1)
+            attn = torch.einsum("bhl,bhld->bhd", p, v).reshape(B, Hq * D)
+            h = h + attn @ L["wo"].float().t()
+            x = norm(h, L["post_norm"])
+            gu = x @ L["wgu"].float().t()
+            act = F.silu(gu[:, :self.I]) * gu[:, self.I:]
+            h = h + act @ L["wd"].float().t()
+            nxt = self.layers[i + 1]["in_norm"] if i + 1 < len(self.layers) else self.final_norm
+            x = norm(h, nxt)
+            out.append(h.clone())
+        return out
 
     def weight_bytes(self) -> int:
         n = sum(t.numel() for L in self.layers for k, t in L.items() if k.startswith("w"))

@@ -89,19 +89,30 @@ def gemm_swiglu(x: torch.Tensor, wgu, out: torch.Tensor | None = None, splits: i
     return out
 
 
+GEMM_AR_MODES = {"auto": 0, "oneshot": 1, "reduce_scatter": 2}
+
+
 def gemm_allreduce_rmsnorm(comm, x: torch.Tensor, wt: torch.Tensor, residual: torch.Tensor,
                            weight: torch.Tensor, eps: float = 1e-5, out: torch.Tensor | None = None,
-                           splits: int = 0) -> torch.Tensor:
+                           splits: int = 0, mode: str = "auto") -> torch.Tensor:
     """Row-parallel layer tail: ``residual += allreduce(x @ wt.T)``; returns
-    ``rmsnorm(residual) * weight``. The GEMM's epilogue stores each finished
-    bf16 output tile into every rank's buffer over NVLink and raises a flag
-    per tile; a second launch waits for the tiles, sums the ranks in rank
-    order, adds the residual and normalises. ``splits=0`` picks the split-K
-    factor (split partials are added on this GPU before the tile is sent)."""
+    ``rmsnorm(residual) * weight``, in two launches.
+
+    ``mode="oneshot"``: the GEMM's epilogue stores each finished bf16 output
+    tile into every rank's buffer over NVLink and raises a flag per tile; the
+    second launch waits for the tiles, sums the ranks in rank order, adds the
+    residual and normalises. ``mode="reduce_scatter"``: the epilogue stores
+    token row ``t`` only into rank ``t % world_size``; the second launch
+    reduces the rows this rank owns, applies residual + norm, and gathers the
+    other owners' new residual rows (about 2/ws of the one-shot's NVLink
+    bytes, one more flag exchange). ``"auto"`` takes the reduce-scatter from
+    8 rows per rank on. ``splits=0`` picks the split-K factor (split partials
+    are added on this GPU before the tile is sent)."""
     if out is None:
         out = torch.empty_like(residual)
     data, _, packed = _operand(wt)
-    comm._ops.gemm_ar_rmsnorm(comm._ptr, x, data, residual, weight, out, float(eps), int(splits), packed)
+    comm._ops.gemm_ar_rmsnorm(comm._ptr, x, data, residual, weight, out, float(eps), int(splits), packed,
+                              GEMM_AR_MODES[mode])
     if comm.env.check and not torch.cuda.is_current_stream_capturing():
         torch.cuda.current_stream().synchronize()
         comm.check()

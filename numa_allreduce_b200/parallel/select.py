@@ -156,11 +156,16 @@ def parse_table(obj: dict) -> list[Entry]:
     return out
 
 
-def build_table(results: list[dict], nccl_key: str = NCCL, hybrid: dict | None = None) -> dict:
+def build_table(results: list[dict], nccl_key: str = NCCL, hybrid: dict | None = None,
+                margin: float = 0.03) -> dict:
     """Builds a table from sweep rows ``{"world_size", "dtype", "nvls", "bytes",
-    "algo", "busbw_gbs"}``: for each size the fastest protocol wins; adjacent
-    sizes with the same winner merge into one step. ``hybrid`` maps a world
-    size to the measured split of the hybrid protocol."""
+    "algo", "busbw_gbs"}``: for each size the fastest protocol wins, except
+    that a protocol within ``margin`` of the winner is kept when it is the
+    previous size's choice or when the winner is NCCL and it is this
+    library's (differences that small are run-to-run noise and would only
+    add steps); adjacent sizes with the same choice merge into one step.
+    ``hybrid`` maps a world size to the measured split of the hybrid
+    protocol."""
     groups: dict[tuple, dict[int, dict[str, float]]] = {}
     for r in results:
         k = (int(r["world_size"]), str(r["dtype"]), bool(r.get("nvls", False)))
@@ -169,7 +174,17 @@ def build_table(results: list[dict], nccl_key: str = NCCL, hybrid: dict | None =
     for (ws, dtype, nvls), by_size in sorted(groups.items()):
         steps: list[list] = []
         for size in sorted(by_size):
-            algo = max(by_size[size].items(), key=lambda kv: kv[1])[0]
+            cands = by_size[size]
+            algo, best = max(cands.items(), key=lambda kv: kv[1])
+            prev = steps[-1][1] if steps else None
+            if prev is not None and prev != algo and cands.get(prev, 0.0) >= (1 - margin) * best:
+                algo = prev
+            elif algo == nccl_key:
+                ours = {a: v for a, v in cands.items() if a != nccl_key}
+                if ours:
+                    a2, v2 = max(ours.items(), key=lambda kv: kv[1])
+                    if v2 >= (1 - margin) * best:
+                        algo = a2
             if steps and steps[-1][1] == algo:
                 steps[-1][0] = size
             else:

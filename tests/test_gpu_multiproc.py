@@ -184,13 +184,21 @@ def _worker_gemm_ar(rank, ws, port):
             res0 = res.clone()
             outs = []
             pw = pack_weight(wt)
-            for splits in ((0, 1, 3) if T <= 16 else (0,)):  # auto, no split-K, an odd split count
-                for w_in in (wt, pw):
-                    for rep in range(2):
-                        res.copy_(res0)
-                        out = gemm_allreduce_rmsnorm(ar, x, w_in, res, norm_w, 1e-5, splits=splits)
-                        torch.cuda.synchronize()
-                    outs.append((splits, res.clone(), out.clone()))
+            for mode in ("oneshot", "reduce_scatter"):
+                for splits in ((0, 1, 3) if T <= 16 else (0,)):  # auto, no split-K, an odd split count
+                    for w_in in (wt, pw):
+                        for rep in range(2):
+                            res.copy_(res0)
+                            out = gemm_allreduce_rmsnorm(ar, x, w_in, res, norm_w, 1e-5, splits=splits, mode=mode)
+                            torch.cuda.synchronize()
+                        outs.append((f"{mode}/{splits}", res.clone(), out.clone()))
+                        if mode == "reduce_scatter":
+                            # every rank holds the same bits of the residual and the output
+                            for name, tns in (("residual", res), ("out", out)):
+                                peers = [torch.empty_like(tns) for _ in range(ws)]
+                                dist.all_gather(peers, tns)
+                                if not all(torch.equal(q, peers[0]) for q in peers):
+                                    errors.append(f"T={T} {mode}/{splits}: ranks disagree on {name}")
             parts = (x.float() @ wt.float().t()).to(torch.bfloat16)  # each rank's partial, as the epilogue rounds it
             gathered = [torch.empty_like(parts) for _ in range(ws)]
             dist.all_gather(gathered, parts)
