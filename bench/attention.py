@@ -8,6 +8,8 @@ around the replays:
 
     rope_attention     this library: RoPE + KV append + attention, one launch
     decode_attention   this library: attention only (q already rotated)
+    *_tc               the same on the tensor cores (tcgen05 scores and
+                       output, TMA-staged K/V chunks of 128 positions)
     sdpa               torch scaled_dot_product_attention (GQA expanded)
 
     python bench/attention.py [--batches 1,8,32] [--context 1024]
@@ -85,6 +87,11 @@ def main():
                                                          Hq, Hkv, splits), a.calls, a.reps)
         t_attn = time_graph(lambda i: ops.decode_attention(q, ks[i % copies], vs[i % copies], pos, out, splits),
                             a.calls, a.reps)
+        sp_tc = a.splits or int(ops.attention_splits_tc(B, Hkv, a.context + 1))
+        t_rope_tc = time_graph(lambda i: ops.rope_attention_tc(qkv, cos, sin, pos, ks[i % copies], vs[i % copies],
+                                                               out, Hq, Hkv, sp_tc), a.calls, a.reps)
+        t_attn_tc = time_graph(lambda i: ops.decode_attention_tc(q, ks[i % copies], vs[i % copies], pos, out,
+                                                                 sp_tc), a.calls, a.reps)
         L = a.context + 1
 
         def sdpa(i):
@@ -95,7 +102,9 @@ def main():
         t_sdpa = time_graph(sdpa, a.calls, a.reps)
         row = {"batch": B, "context": a.context, "splits": splits, "kv_mb": round(kv_bytes / 1e6, 2),
                "rope_attention_us": round(t_rope, 2), "decode_attention_us": round(t_attn, 2),
-               "sdpa_us": round(t_sdpa, 2), "attn_tbs": round(kv_bytes / t_attn / 1e6, 3)}
+               "sdpa_us": round(t_sdpa, 2), "attn_tbs": round(kv_bytes / t_attn / 1e6, 3),
+               "splits_tc": sp_tc, "rope_attention_tc_us": round(t_rope_tc, 2),
+               "decode_attention_tc_us": round(t_attn_tc, 2), "attn_tc_tbs": round(kv_bytes / t_attn_tc / 1e6, 3)}
         print(json.dumps(row), flush=True)
         del ks, vs
         torch.cuda.empty_cache()

@@ -36,6 +36,7 @@ def parse():
     p.add_argument("--layers", type=int, default=80)
     p.add_argument("--model", default="70b", choices=["70b", "8b", "tiny"])
     p.add_argument("--impls", default="fused,baseline")
+    p.add_argument("--attention", default="tc", choices=["tc", "simt"])
     p.add_argument("--reps", type=int, default=20)
     p.add_argument("--shard-as", type=int, default=None,
                    help="single GPU: decode one rank's shard of an N-way TP model (no allreduce)")
@@ -84,7 +85,8 @@ def main():
     comm = NumaAwareAllReduce(dist.group.WORLD, device=local, fused_bytes=32 << 20)
     rows = []
     for B in [int(b) for b in args.batches.split(",")]:
-        model = LlamaTPDecoder(cfg, comm, batch=B, context=args.context, shard_of=args.shard_as)
+        model = LlamaTPDecoder(cfg, comm, batch=B, context=args.context, shard_of=args.shard_as,
+                               attention=args.attention)
         model.tokens.copy_(torch.arange(B, device="cuda") * 7 + 3)
         row = {"batch": B, "world_size": world, "context": args.context, "layers": cfg.layers,
                "weight_gb_per_rank": round(model.weight_bytes() / 1e9, 2)}

@@ -76,18 +76,21 @@ def main():
     p.add_argument("--context", type=int, default=1024)
     p.add_argument("--reps", type=int, default=20)
     p.add_argument("--impl", default="fused")
+    p.add_argument("--attention", default="tc", choices=["tc", "simt"])
     a = p.parse_args()
     cfg = LlamaConfig.llama3_70b()
     cfg.layers = a.layers
-    model = LlamaTPDecoder(cfg, None, batch=a.batch, context=a.context, impl=a.impl, shard_of=a.tp)
+    model = LlamaTPDecoder(cfg, None, batch=a.batch, context=a.context, impl=a.impl, shard_of=a.tp,
+                           attention=a.attention)
     real_ops = model.ops
     real_norm = llama_tp.rmsnorm_residual
-    out = {"batch": a.batch, "layers": a.layers, "tp": a.tp, "impl": a.impl}
+    out = {"batch": a.batch, "layers": a.layers, "tp": a.tp, "impl": a.impl, "attention": a.attention}
+    attn_ops = ["rope_append", "decode_attention", "rope_attention", "rope_attention_tc"]
     variants = {
         "full": ([], False),
-        "no_attention": (["rope_append", "decode_attention", "rope_attention"], False),
+        "no_attention": (attn_ops, False),
         "no_norm": ([], True),
-        "gemm_only": (["rope_append", "decode_attention", "rope_attention", "silu_mul"], True),
+        "gemm_only": (attn_ops + ["silu_mul"], True),
     }
     for name, (skip, no_norm) in variants.items():
         model.ops = _Skip(real_ops, skip)

@@ -198,6 +198,8 @@ def main():
             from numa_allreduce_b200.utils.timing import pci_bus_id
 
             counters = NvlinkCounters(pci_bus_id(local))
+            counters.read()
+            print(f"NVLink counters: links {counters.links}, diagnostics {counters.diag}", flush=True)
         except Exception as e:  # counters are optional
             print(f"NVLink counters unavailable: {e}", flush=True)
     sizes = [int(v) for v in args.sizes.split(",")]

@@ -399,8 +399,7 @@ __device__ __forceinline__ void twoshot_pipe_body(const ARParams& p, const RankV
           }
         }
       }
-      named_barrier(1, nt);
-      if (*abort_flag) break;
+      if (named_barrier_or(1, nt, *abort_flag != 0)) break;
       const int64_t tb = (c + k * C) * tile;
       int len[WS - 1];
 #pragma unroll
@@ -436,8 +435,7 @@ __device__ __forceinline__ void twoshot_pipe_body(const ARParams& p, const RankV
         ok = wait_geq_cta(&mypad->flags[kFlagPipeRS].v[c][peers[t]], make_seq(epoch, k + 1), w, peers[t], kStageRS,
                           abort_flag);
       if (!ok) *abort_flag = 1;
-      named_barrier(2, nt);
-      if (*abort_flag) break;
+      if (named_barrier_or(2, nt, *abort_flag != 0)) break;
       const int64_t tb = (c + k * C) * tile;
       const int64_t mb = tb + static_cast<int64_t>(rank) * chp;
       const int mlen = chunk_len(tb, rank);
@@ -481,8 +479,7 @@ __device__ __forceinline__ void twoshot_pipe_body(const ARParams& p, const RankV
         ok = wait_geq_cta(&mypad->flags[kFlagPipeAG].v[c][peers[t]], make_seq(epoch, k + 1), w, peers[t], kStageAG,
                           abort_flag);
       if (!ok) *abort_flag = 1;
-      named_barrier(3, nt);
-      if (*abort_flag) break;
+      if (named_barrier_or(3, nt, *abort_flag != 0)) break;
       const int64_t tb = (c + k * C) * tile;
       int len[WS - 1];
 #pragma unroll
@@ -809,8 +806,7 @@ __device__ __forceinline__ void nvls_twoshot_body(const ARParams& p, const RankV
           }
         }
       }
-      named_barrier(1, nt);
-      if (*abort_flag) break;
+      if (named_barrier_or(1, nt, *abort_flag != 0)) break;
       const int64_t tb = (c + k * C) * tile;
       const int tlen = static_cast<int>(span_len(tile, npacks - tb));
       uint4* us = ucb + slot * slot_packs;
@@ -837,8 +833,7 @@ __device__ __forceinline__ void nvls_twoshot_body(const ARParams& p, const RankV
       const int slot = g % S;
       const uint32_t target = WS * (g / S + 1u);
       if (t == 0 && !pipe_wait(&upad->pipe[c][slot][0][0], target, w, abort_flag, kStageNvls1)) *abort_flag = 1;
-      named_barrier(2, nt);
-      if (*abort_flag) break;
+      if (named_barrier_or(2, nt, *abort_flag != 0)) break;
       fence_proxy_alias();  // unicast acquire before multicast loads
       const int64_t mb = (c + k * C) * tile + static_cast<int64_t>(rank) * chp;
       const int mlen = static_cast<int>(span_len(chp, npacks - mb));
@@ -869,8 +864,7 @@ __device__ __forceinline__ void nvls_twoshot_body(const ARParams& p, const RankV
       const int slot = g % S;
       const uint32_t target = WS * (g / S + 1u);
       if (t == 0 && !pipe_wait(&upad->pipe[c][slot][1][0], target, w, abort_flag, kStageNvls2)) *abort_flag = 1;
-      named_barrier(3, nt);
-      if (*abort_flag) break;
+      if (named_barrier_or(3, nt, *abort_flag != 0)) break;
       fence_proxy_alias();  // the owners' multicast stores before unicast loads
       const int64_t tb = (c + k * C) * tile;
       const int tlen = static_cast<int>(span_len(tile, npacks - tb));

@@ -173,6 +173,19 @@ NAB_DINLINE uint32_t ld_volatile_u32(const uint32_t* p) {
 NAB_DINLINE void st_volatile_u32(uint32_t* p, uint32_t v) {
   asm volatile("st.volatile.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+// Named barrier over `n` threads that also ORs a predicate over them: every
+// participating thread gets the same answer, so a group can leave a loop
+// together even when a flag it reads may change while its threads arrive.
+NAB_DINLINE bool named_barrier_or(int id, int n, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n barrier.red.or.pred q, %2, %3, p;\n selp.u32 %0, 1, 0, q;\n}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+
 // Programmatic dependent launch: lets a kernel launched after this one with
 // programmatic stream serialization begin scheduling now (it waits for this
 // grid's completion before it reads anything this grid writes).

@@ -526,8 +526,10 @@ int gemm_active_clusters(int bn, int cs) { return active_clusters(bn, cs); }
 int gemm_ar_mode_for(int T, int ws) {
   // One-shot: every rank's whole output crosses to every peer ((ws - 1) T H
   // elements per direction) but needs no second exchange; reduce-scatter +
-  // gather moves 2 (ws - 1) / ws T H and adds one flag round trip. From a few
-  // rows per rank on, the bytes win.
+  // gather moves 2 (ws - 1) / ws T H and adds one flag round trip. At two
+  // ranks both move the same bytes (measured: one-shot faster at every T);
+  // from four ranks on, the bytes win once there are a few rows per rank.
+  if (ws <= 2) return kGemmArOneshot;
   return T >= 8 * ws ? kGemmArReduceScatter : kGemmArOneshot;
 }
 

@@ -457,6 +457,40 @@ void rope_attention_op(const at::Tensor& qkv, const at::Tensor& cos, const at::T
                       static_cast<int>(k_cache.size(2)), static_cast<int>(splits));
 }
 
+void decode_attention_tc_op(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
+                            const at::Tensor& pos, at::Tensor& out, int64_t splits) {
+  TORCH_CHECK(q.dim() == 3 && q.size(2) == 128 && k_cache.dim() == 4 && k_cache.size(3) == 128 && q.is_contiguous() &&
+                  k_cache.is_contiguous() && v_cache.is_contiguous() && v_cache.sizes() == k_cache.sizes(),
+              "decode_attention_tc: shapes");
+  const int64_t B = q.size(0), Hq = q.size(1), Hkv = k_cache.size(1);
+  const at::cuda::OptionalCUDAGuard guard(q.device());
+  nab::decode_attention_tc(at::cuda::getCurrentCUDAStream().stream(), q.data_ptr(), k_cache.data_ptr(),
+                           v_cache.data_ptr(), pos.data_ptr<int>(), out.data_ptr(), static_cast<int>(B),
+                           static_cast<int>(Hq), static_cast<int>(Hkv), static_cast<int>(k_cache.size(2)),
+                           static_cast<int>(splits));
+}
+
+void rope_attention_tc_op(const at::Tensor& qkv, const at::Tensor& cos, const at::Tensor& sin, const at::Tensor& pos,
+                          at::Tensor& k_cache, at::Tensor& v_cache, at::Tensor& out, int64_t Hq, int64_t Hkv,
+                          int64_t splits) {
+  TORCH_CHECK(qkv.dim() == 2 && qkv.size(1) == (Hq + 2 * Hkv) * 128 && qkv.is_contiguous(), "rope_attention_tc: qkv");
+  TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(1) == Hkv && k_cache.size(3) == 128 && k_cache.is_contiguous() &&
+                  v_cache.is_contiguous() && v_cache.sizes() == k_cache.sizes() && cos.scalar_type() == at::kFloat,
+              "rope_attention_tc: shapes");
+  const at::cuda::OptionalCUDAGuard guard(qkv.device());
+  nab::rope_attention_tc(at::cuda::getCurrentCUDAStream().stream(), qkv.data_ptr(), cos.data_ptr<float>(),
+                         sin.data_ptr<float>(), pos.data_ptr<int>(), k_cache.data_ptr(), v_cache.data_ptr(),
+                         out.data_ptr(), static_cast<int>(qkv.size(0)), static_cast<int>(Hq), static_cast<int>(Hkv),
+                         static_cast<int>(k_cache.size(2)), static_cast<int>(splits));
+}
+
+int64_t attention_splits_tc(int64_t B, int64_t Hkv, int64_t context) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return nab::attention_splits_tc(static_cast<int>(B), static_cast<int>(Hkv), static_cast<int>(context), sms);
+}
+
 int64_t attention_splits(int64_t B, int64_t Hkv, int64_t context) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -554,6 +588,12 @@ TORCH_LIBRARY(nab, m) {
   m.impl("rope_attention", c10::kCUDA, &rope_attention_op);
   m.def("attention_splits(int B, int Hkv, int context) -> int", &attention_splits);
   m.impl("decode_attention", c10::kCUDA, &decode_attention_op);
+  m.def("decode_attention_tc(Tensor q, Tensor k_cache, Tensor v_cache, Tensor pos, Tensor(a!) out, int splits) -> ()");
+  m.impl("decode_attention_tc", c10::kCUDA, &decode_attention_tc_op);
+  m.def("rope_attention_tc(Tensor qkv, Tensor cos, Tensor sin, Tensor pos, Tensor(a!) k_cache, Tensor(b!) v_cache, "
+        "Tensor(c!) out, int Hq, int Hkv, int splits) -> ()");
+  m.impl("rope_attention_tc", c10::kCUDA, &rope_attention_tc_op);
+  m.def("attention_splits_tc(int B, int Hkv, int context) -> int", &attention_splits_tc);
   m.def("silu_mul(Tensor gu, Tensor(a!) out) -> ()");
   m.impl("silu_mul", c10::kCUDA, &silu_mul_op);
   m.def("rmsnorm_residual(Tensor inp, Tensor(a!) residual, Tensor weight, Tensor(b!) out, float eps) -> ()");

@@ -89,10 +89,15 @@ class LlamaTPDecoder:
         shard_of: with a single GPU, build the shard of a ``shard_of``-way
             tensor-parallel model (same per-GPU shapes, no allreduce), to
             study one rank's kernels alone.
+        attention: ``"tc"`` for the tensor-core decode attention (tcgen05
+            scores and output per 128-position chunk), ``"simt"`` for the
+            SIMT kernel; the fused variant only (the baseline uses the
+            two-launch SIMT path).
     """
 
     def __init__(self, cfg: LlamaConfig, comm, batch: int, context: int, impl: str = "fused", seed: int = 0,
-                 device: torch.device | str = "cuda", attn_splits: int | None = None, shard_of: int | None = None):
+                 device: torch.device | str = "cuda", attn_splits: int | None = None, shard_of: int | None = None,
+                 attention: str = "tc"):
         if impl not in ("fused", "baseline"):
             raise ValueError("impl must be 'fused' or 'baseline'")
         self.cfg, self.comm, self.impl = cfg, comm, impl
@@ -156,7 +161,11 @@ class LlamaTPDecoder:
         self.act = torch.empty(batch, self.I, **bf)
         self.y = torch.empty(batch, H, **bf)
         self.logits = torch.empty(batch, self.v_local, **bf)
+        if attention not in ("tc", "simt"):
+            raise ValueError("attention must be 'tc' (tensor cores) or 'simt'")
+        self.attention = attention
         self.splits = attn_splits or int(self.ops.attention_splits(batch, self.Hkv, context + 1))
+        self.splits_tc = attn_splits or int(self.ops.attention_splits_tc(batch, self.Hkv, context + 1))
         self.gemm_splits = {}
         self.next_tokens = torch.zeros(batch, device=self.device, dtype=torch.long)
         self._gathered = torch.empty(W * batch * 2, device=self.device, dtype=torch.float32)
@@ -217,6 +226,9 @@ class LlamaTPDecoder:
             if self.impl == "baseline":
                 ops.rope_append(self.qkv, self.cos, self.sin, self.pos, self.q, L["k"], L["v"], self.Hq, self.Hkv)
                 ops.decode_attention(self.q, L["k"], L["v"], self.pos, attn, self.splits)
+            elif self.attention == "tc":
+                ops.rope_attention_tc(self.qkv, self.cos, self.sin, self.pos, L["k"], L["v"], attn, self.Hq,
+                                      self.Hkv, self.splits_tc)
             else:
                 ops.rope_attention(self.qkv, self.cos, self.sin, self.pos, L["k"], L["v"], attn, self.Hq, self.Hkv,
                                    self.splits)

@@ -38,6 +38,7 @@ CORE_SOURCES = [
     "nab_fused.cu",
     "nab_gemm_sm100.cu",
     "nab_llama.cu",
+    "nab_attn_sm100.cu",
     "nab_comm.cpp",
     "nab_kerr.cpp",
     "nab_nvls.cpp",

@@ -32,12 +32,19 @@ class NvlinkCounters:
         else:
             self.h = pynvml.nvmlDeviceGetHandleByIndex(index or 0)
         self.links = []
+        self.diag: dict[str, object] = {}
         for link in range(MAX_LINKS):
             try:
-                if pynvml.nvmlDeviceGetNvLinkState(self.h, link) == pynvml.NVML_FEATURE_ENABLED:
-                    self.links.append(link)
-            except pynvml.NVMLError:
-                break
+                state = pynvml.nvmlDeviceGetNvLinkState(self.h, link)
+            except pynvml.NVMLError as e:
+                self.diag.setdefault("state_errors", []).append((link, str(e)))
+                continue
+            if state == pynvml.NVML_FEATURE_ENABLED:
+                self.links.append(link)
+        if not self.links:
+            # no per-link state: query every possible link and keep the ones
+            # whose counters answer
+            self.links = list(range(MAX_LINKS))
         nv = pynvml
         self.families = {
             "data_kib": (getattr(nv, "NVML_FI_DEV_NVLINK_THROUGHPUT_DATA_TX", None),
@@ -47,33 +54,37 @@ class NvlinkCounters:
         }
 
     def read(self) -> dict[str, tuple[int, int] | None]:
-        """Cumulative (tx_bytes, rx_bytes) per counter family, summed over links."""
+        """Cumulative (tx_bytes, rx_bytes) per counter family, summed over the
+        links whose counters answered."""
         out = {}
         for name, (tx_id, rx_id, unit) in self.families.items():
-            if tx_id is None or rx_id is None or not self.links:
+            if tx_id is None or rx_id is None:
                 out[name] = None
                 continue
             ids = [(tx_id, l) for l in self.links] + [(rx_id, l) for l in self.links]
             try:
                 vals = self.nv.nvmlDeviceGetFieldValues(self.h, ids)
-            except self.nv.NVMLError:
+            except self.nv.NVMLError as e:
+                self.diag[name] = str(e)
                 out[name] = None
                 continue
             tx = rx = 0
-            ok = True
+            answered = 0
             n = len(self.links)
+            codes = []
             for i, v in enumerate(vals):
+                codes.append(int(v.nvmlReturn))
                 if v.nvmlReturn != 0:
-                    ok = False
-                    break
+                    continue
+                answered += 1
                 x = int(v.value.ullVal) * unit
                 if i < n:
                     tx += x
                 else:
                     rx += x
-            out[name] = (tx, rx) if ok else None
+            self.diag[name + "_codes"] = sorted(set(codes))
+            out[name] = (tx, rx) if answered else None
         return out
-
 
 def delta(before: dict, after: dict, calls: int = 1) -> dict[str, tuple[float, float] | None]:
     """Bytes per call (tx, rx) between two reads."""

@@ -142,3 +142,51 @@ def test_decode_depth_against_fp32():
     for row in res["per_layer"]:
         assert row["fused_vs_fp32"] < 5e-2, row
         assert row["fused_vs_fp32"] < 2.0 * row["baseline_vs_fp32"] + 1e-2, row
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,L,splits", [(1, 8, 1, 1025, 16), (4, 16, 8, 300, 2), (2, 8, 2, 64, 1),
+                                              (1, 8, 1, 3, 1), (32, 8, 1, 1025, 0), (2, 4, 4, 130, 1),
+                                              (3, 6, 2, 700, 4)])
+def test_decode_attention_tensor_cores(B, Hq, Hkv, L, splits):
+    """tcgen05 scores (K . Q^T) and output (V^T . P^T) per 128-position chunk
+    against the fp32 PyTorch reference; ragged last chunks, several groups."""
+    ops = _ext.load()
+    Lmax = ((L + 63) // 64) * 64
+    g = torch.Generator(device="cuda").manual_seed(5)
+    q = torch.randn(B, Hq, 128, generator=g, device="cuda").to(torch.bfloat16)
+    k = torch.randn(B, Hkv, Lmax, 128, generator=g, device="cuda").to(torch.bfloat16)
+    v = torch.randn(B, Hkv, Lmax, 128, generator=g, device="cuda").to(torch.bfloat16)
+    pos = torch.tensor([L - 1], device="cuda", dtype=torch.int32)
+    splits = splits or int(ops.attention_splits_tc(B, Hkv, L))
+    ref = reference_attention(q, k, v, L)
+    for _ in range(2):
+        out = torch.zeros(B, Hq, 128, device="cuda", dtype=torch.bfloat16)
+        ops.decode_attention_tc(q, k, v, pos, out, splits)
+        torch.cuda.synchronize()
+        torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,pos,splits", [(1, 8, 1, 1024, 8), (3, 8, 2, 40, 1), (2, 8, 1, 0, 1),
+                                                (2, 8, 1, 255, 2)])
+def test_rope_attention_tensor_cores(B, Hq, Hkv, pos, splits):
+    """RoPE + KV append + tensor-core attention == rope_append, then the
+    fp32 reference; the cache rows written match rope_append's."""
+    ops = _ext.load()
+    D, Lmax = 128, ((pos + 1 + 63) // 64) * 64
+    g = torch.Generator(device="cuda").manual_seed(9)
+    qkv = torch.randn(B, (Hq + 2 * Hkv) * D, generator=g, device="cuda").to(torch.bfloat16)
+    k0 = torch.randn(B, Hkv, Lmax, D, generator=g, device="cuda").to(torch.bfloat16)
+    v0 = torch.randn(B, Hkv, Lmax, D, generator=g, device="cuda").to(torch.bfloat16)
+    inv = 1.0 / (500000.0 ** (torch.arange(0, D, 2, device="cuda", dtype=torch.float64) / D))
+    ang = torch.arange(Lmax, device="cuda", dtype=torch.float64)[:, None] * inv[None, :]
+    cos, sin = ang.cos().float().contiguous(), ang.sin().float().contiguous()
+    p = torch.tensor([pos], device="cuda", dtype=torch.int32)
+    k1, v1 = k0.clone(), v0.clone()
+    q = torch.empty(B, Hq, D, device="cuda", dtype=torch.bfloat16)
+    ops.rope_append(qkv, cos, sin, p, q, k1, v1, Hq, Hkv)
+    k2, v2 = k0.clone(), v0.clone()
+    out = torch.empty(B, Hq, D, device="cuda", dtype=torch.bfloat16)
+    ops.rope_attention_tc(qkv, cos, sin, p, k2, v2, out, Hq, Hkv, splits)
+    torch.cuda.synchronize()
+    assert torch.equal(k1, k2) and torch.equal(v1, v2)
+    torch.testing.assert_close(out.float(), reference_attention(q, k1, v1, pos + 1), rtol=2e-2, atol=2e-2)
