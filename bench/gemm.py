@@ -45,6 +45,9 @@ def parse():
     p.add_argument("--reps", type=int, default=5)
     p.add_argument("--splits", type=int, default=0, help="force a split count (0: the heuristic)")
     p.add_argument("--no-pdl", action="store_true", help="launch the GEMMs without programmatic dependent launch")
+    p.add_argument("--split-sweep", action="store_true",
+                   help="time the packed-weight GEMM at every split count 1..16 and report the best against "
+                        "the heuristic's choice")
     p.add_argument("--out", default=None)
     return p.parse_args()
 
@@ -91,6 +94,21 @@ def main():
             x = torch.randn(T, K, device=dev, dtype=torch.bfloat16)
             y = torch.empty(T, N, device=dev, dtype=torch.bfloat16)
             splits = a.splits or int(ops.gemm_splits(T, N, K))
+            if a.split_sweep:
+                kb = K // 64
+                times = {}
+                for sp in range(1, 17):
+                    per = -(-kb // sp)
+                    if -(-kb // per) != sp:  # a split without work: not a launchable count
+                        continue
+                    times[sp] = round(time_graph(lambda i: gemm(x, wps[i % copies], out=y, splits=sp), a.calls,
+                                                 a.reps), 2)
+                best = min(times, key=times.get)
+                row = {"shape": name, "T": T, "auto_splits": splits, "auto_us": times.get(splits),
+                       "best_splits": best, "best_us": times[best], "times_us": times}
+                rows.append(row)
+                print(json.dumps(row), flush=True)
+                continue
             ref = F.linear(x, ws[0]).float()
             err = (gemm(x, ws[0], out=y, splits=splits).float() - ref).abs().max().item()
             err_p = (gemm(x, wps[0], out=y, splits=splits).float() - ref).abs().max().item()

@@ -56,6 +56,8 @@ def parse():
     p.add_argument("--hier-groups", default=None, help="e.g. 0,1,2,3|4,5,6,7")
     p.add_argument("--pipe-configs", default=None,
                    help="extra pipelined two-shot configurations to time, e.g. 148x256,128x512 (CTAs x tile KiB)")
+    p.add_argument("--oneshot-configs", default=None,
+                   help="extra one-shot launch shapes to time up to 1 MiB, e.g. 256x64,512x32 (packs per CTA x max CTAs)")
     p.add_argument("--hybrid-configs", default=None,
                    help="hybrid splits to time, e.g. 400x64x80,300x56x88 (P2P per mille x P2P CTAs x NVLS CTAs); "
                         "--write-table keeps the one with the best bus bandwidth summed over sizes >= 16 MiB")
@@ -202,6 +204,13 @@ def main():
             print(f"NVLink counters: links {counters.links}, diagnostics {counters.diag}", flush=True)
         except Exception as e:  # counters are optional
             print(f"NVLink counters unavailable: {e}", flush=True)
+    oneshot_extra = []
+    if args.oneshot_configs:
+        for spec in args.oneshot_configs.split(","):
+            grain, ctas = (int(v) for v in spec.split("x"))
+            oneshot_extra.append((f"oneshot_{grain}x{ctas}",
+                                  NumaAwareAllReduce(dist.group.WORLD, device=local, use_nvls=False,
+                                                     oneshot_grain=grain, oneshot_ctas=ctas)))
     sizes = [int(v) for v in args.sizes.split(",")]
     if args.algos == "all":
         algos = ["oneshot", "twoshot", "twoshot_pipe"] + (
@@ -233,6 +242,9 @@ def main():
                               (lambda nm=name: ar.all_reduce(x, out=out, algo=nm)), True))
             for label, comm in extra:
                 cands.append((label, (lambda c=comm: c.all_reduce(x, out=out, algo="twoshot_pipe")), True))
+            if size <= args.max_oneshot:
+                for label, comm in oneshot_extra:
+                    cands.append((label, (lambda c=comm: c.all_reduce(x, out=out, algo="oneshot")), True))
             if args.hybrid_configs and ar.has_nvls:
                 for spec in args.hybrid_configs.split(","):
                     split = tuple(int(v) for v in spec.split("x"))
@@ -287,7 +299,8 @@ def main():
         if args.write_table:
             tab_rows = [dict(r, algo=r["algo"].split(":")[-1] if r["algo"].startswith("auto:") else r["algo"])
                         for r in rows
-                        if r["mode"] == "eager" and r["correct"] and not r["algo"].startswith(("ref", "pipe_"))]
+                        if r["mode"] == "eager" and r["correct"]
+                        and not r["algo"].startswith(("ref", "pipe_", "oneshot_"))]
             split, tab_rows = pick_hybrid(tab_rows)
             table = build_table(tab_rows, hybrid={world: split} if split else None)
             if args.merge and os.path.exists(args.write_table):
@@ -296,7 +309,7 @@ def main():
                 json.dump(table, f, indent=1)
     torch.cuda.synchronize()
     ar.close()
-    for _, comm in extra:
+    for _, comm in extra + oneshot_extra:
         comm.close()
     if ref is not None:
         ref.close()

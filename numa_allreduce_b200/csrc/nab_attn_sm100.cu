@@ -5,10 +5,12 @@
 // covers a contiguous range of positions in chunks of 128. Per chunk:
 //   producer (warp 0, one thread)  TMA-loads the K and V chunk, 128 rows x
 //       128 dims each, as two 64-dim boxes with 128-byte swizzle, into a
-//       2-stage ring (mbarrier complete_tx);
+//       3-stage ring (mbarrier complete_tx);
 //   scores   S^T[128 positions x 16 heads] = K . Q^T: 8 tcgen05.mma
 //       (M=128, N=16, K=16), A = K (K-major), B = Q (the group's <= 8 query
-//       heads, rows 8-15 zero), fp32 accumulator in TMEM columns 0-15;
+//       heads, rows 8-15 zero), fp32 accumulator in TMEM columns 0-15 or
+//       16-31 by chunk parity: the next chunk's scores are issued as soon as
+//       this chunk's are read, so they run during this chunk's softmax;
 //   softmax  4 warps read S from TMEM (one position per thread), mask
 //       positions past the range, update the running max / sum per head
 //       (warp shuffles + shared memory), write P (bf16) as a K-major tile;
@@ -49,14 +51,14 @@ namespace {
 
 constexpr int kD = 128;                  // head dim
 constexpr int kTc = 128;                 // positions per chunk (the scores MMA's M)
-constexpr int kStages = 2;               // K/V ring depth
+constexpr int kStages = 3;               // K/V ring depth (3 x 64 KB: a split's first chunks load at once)
 constexpr int kBox = kTc * 128;          // one TMA box: 128 rows x 64 dims (128 bytes)
 constexpr int kStageBytes = 4 * kBox;    // K dims 0-63 | K 64-127 | V 0-63 | V 64-127
 constexpr int kTileBytes = 16 * 128;     // Q or P: 16 rows x 64 elements, one swizzle tile
 constexpr int kSmemTc = kStages * kStageBytes + 4 * kTileBytes + 1024;
 constexpr int kThreadsTc = 160;          // warp 0: TMA producer; warps 1-4: MMA, softmax, output
 constexpr int kMaxSplitsTc = 16;
-constexpr uint32_t kTmemCols = 64;       // S in columns 0-15, O in 32-47
+constexpr uint32_t kTmemCols = 64;       // S in columns 0-15 / 16-31 (chunk parity), O in 32-47
 
 struct AttnTcArgs {
   const __nv_bfloat16* q;  // [B, q_stride]: q heads at 0 (kRope: the qkv projection)
@@ -112,7 +114,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   uint8_t* ps = qs + 2 * kTileBytes;             // P tiles: positions 0-63 | 64-127
   __shared__ __align__(8) uint64_t full_bar[kStages];
   __shared__ __align__(8) uint64_t empty_bar[kStages];
-  __shared__ __align__(8) uint64_t mma_bar;
+  __shared__ __align__(8) uint64_t mma_bar;   // scores of a chunk done (one phase per chunk)
+  __shared__ __align__(8) uint64_t out_bar;   // output MMAs of a chunk done
   __shared__ __align__(8) uint64_t kvnew_bar;
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
@@ -132,6 +135,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       sm100::mbar_init(&empty_bar[s], 1);
     }
     sm100::mbar_init(&mma_bar, 1);
+    sm100::mbar_init(&out_bar, 1);
     sm100::mbar_init(&kvnew_bar, 1);
     sm100::fence_barrier_init();
     s_abort = 0;
@@ -286,45 +290,60 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       l[h] = 0.f;
       acc[h] = 0.f;
     }
+    // S^T = K . Q^T of chunk j into TMEM columns 16 (j & 1) .. + 15 (thread 0
+    // of the group, once the chunk's stage landed), committed to mma_bar: one
+    // phase per chunk. Waits on this CTA's own MMAs use `never` so that no MMA
+    // is still in flight when the CTA leaves.
+    volatile int never = 0;
+    auto scores_mma = [&](int j) {
+      sm100::tc_fence_after();
+      const uint32_t ka = sm100::smem_u32(ring + (j % kStages) * kStageBytes), qa = sm100::smem_u32(qs);
+#pragma unroll
+      for (int k = 0; k < kD / 16; ++k) {
+        const uint32_t off = (k >> 2) * kBox + (k & 3) * 32;
+        const uint32_t qoff = (k >> 2) * kTileBytes + (k & 3) * 32;
+        sm100::mma_bf16(tmem + 16 * (j & 1), sm100::smem_desc_k_sw128(ka + off), sm100::smem_desc_k_sw128(qa + qoff),
+                        idesc_s, k != 0);
+      }
+      sm100::mma_commit(&mma_bar);
+    };
+    // blocking: waits (bounded) for the stage; false, after recording, if it never landed
+    auto issue_scores = [&](int j) -> bool {
+      if (!sm100::mbar_wait(&full_bar[j % kStages], (j / kStages) & 1, a.timeout_ns, abort_flag)) {
+        fail(j);
+        return false;
+      }
+      scores_mma(j);
+      return true;
+    };
+    bool pending = false;  // thread 0: the scores of chunk i were issued
     for (int i = 0; i < nchunks; ++i) {
       const int s = i % kStages;
       uint8_t* st = ring + s * kStageBytes;
       const int c0 = beg + i * kTc, n = min(kTc, end - c0);
-      if (ct == 0 && !sm100::mbar_wait(&full_bar[s], (i / kStages) & 1, a.timeout_ns, abort_flag)) fail(i);
-      if (agreed_abort()) break;
-      if (n < kTc) {
-        // rows past the range: P is zero there, and V must not hold NaN
-        for (int r = n + (ct >> 4); r < kTc; r += 8) {
-          reinterpret_cast<uint4*>(st + 2 * kBox + r * 128)[ct & 7] = make_uint4(0u, 0u, 0u, 0u);
-          reinterpret_cast<uint4*>(st + 3 * kBox + r * 128)[ct & 7] = make_uint4(0u, 0u, 0u, 0u);
-        }
-        fence_async_shared();
-        named_sync(1, 128);
-      }
-      // S^T = K . Q^T
+      // scores of chunk i (phase i of mma_bar), issued now unless issued early
       if (ct == 0) {
-        sm100::tc_fence_after();
-        const uint32_t ka = sm100::smem_u32(st), qa = sm100::smem_u32(qs);
-#pragma unroll
-        for (int j = 0; j < kD / 16; ++j) {
-          const uint32_t off = (j >> 2) * kBox + (j & 3) * 32;
-          const uint32_t qoff = (j >> 2) * kTileBytes + (j & 3) * 32;
-          sm100::mma_bf16(tmem, sm100::smem_desc_k_sw128(ka + off), sm100::smem_desc_k_sw128(qa + qoff), idesc_s,
-                          j != 0);
-        }
-        sm100::mma_commit(&mma_bar);
-        if (!sm100::mbar_wait(&mma_bar, 0, a.timeout_ns, abort_flag)) fail(i);
+        if (!pending && !*abort_flag) pending = issue_scores(i);
+        if (pending && !sm100::mbar_wait(&mma_bar, i & 1, a.timeout_ns, &never)) fail(i);
+        pending = false;
         sm100::tc_fence_before();
       }
       if (agreed_abort()) break;
       sm100::tc_fence_after();
       uint32_t r[16];
-      sm100::tmem_ld16(tmem + t_lane, r);
+      sm100::tmem_ld16(tmem + t_lane + 16 * (i & 1), r);
       sm100::tmem_wait_ld();
       float p[8];
       const bool valid = row < n;
 #pragma unroll
       for (int h = 0; h < 8; ++h) p[h] = (valid && h < G) ? __uint_as_float(r[h]) * a.scale : -INFINITY;
+      if (n < kTc) {
+        // rows past the range: P is zero there, and V must not hold NaN
+        for (int rr = n + (ct >> 4); rr < kTc; rr += 8) {
+          reinterpret_cast<uint4*>(st + 2 * kBox + rr * 128)[ct & 7] = make_uint4(0u, 0u, 0u, 0u);
+          reinterpret_cast<uint4*>(st + 3 * kBox + rr * 128)[ct & 7] = make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
       // chunk max per head
       float mx[8];
 #pragma unroll
@@ -339,7 +358,14 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         for (int h = 0; h < 8; ++h) s_red[q4][h] = mx[h];
       }
       sm100::tc_fence_before();
-      named_sync(1, 128);
+      named_sync(1, 128);  // every thread has read S(i): its TMEM buffer is free
+      // scores of chunk i + 1 run on the tensor cores during this softmax, if
+      // its stage has landed already (otherwise at the top of the next chunk)
+      if (ct == 0 && i + 1 < nchunks && !*abort_flag &&
+          sm100::mbar_try_wait(&full_bar[(i + 1) % kStages], ((i + 1) / kStages) & 1)) {
+        scores_mma(i + 1);
+        pending = true;
+      }
       float alpha[8];
 #pragma unroll
       for (int h = 0; h < 8; ++h) {
@@ -368,13 +394,13 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
         sm[h] = v;
       }
-      fence_async_shared();
-      named_sync(1, 128);  // every thread has read s_red (max) and written P
+      fence_async_shared();  // P and the zeroed V rows, before the tensor core reads them
+      named_sync(1, 128);    // every thread has read s_red (max) and written P
       if (lane == 0) {
 #pragma unroll
         for (int h = 0; h < 8; ++h) s_red[q4][h] = sm[h];
       }
-      // O^T = V^T . P^T
+      // O^T = V^T . P^T (the commit also covers the scores issued above)
       if (ct == 0) {
         sm100::tc_fence_after();
         const uint32_t va = sm100::smem_u32(st + 2 * kBox), pa = sm100::smem_u32(ps);
@@ -384,9 +410,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
           sm100::mma_bf16(tmem + 32, smem_desc_mn_sw128(va + j * 16 * 128, kBox, 1024),
                           sm100::smem_desc_k_sw128(pa + poff), idesc_o, j != 0);
         }
-        sm100::mma_commit(&mma_bar);
+        sm100::mma_commit(&out_bar);
         sm100::mma_commit(&empty_bar[s]);  // the stage is free once these MMAs completed
-        if (!sm100::mbar_wait(&mma_bar, 1, a.timeout_ns, abort_flag)) fail(i);
+        if (!sm100::mbar_wait(&out_bar, i & 1, a.timeout_ns, &never)) fail(i);
         sm100::tc_fence_before();
       }
       if (agreed_abort()) break;
@@ -401,7 +427,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
 #pragma unroll
       for (int h = 0; h < 8; ++h) acc[h] = acc[h] * alpha[h] + __uint_as_float(r[h]);
       sm100::tc_fence_before();
-      named_sync(1, 128);  // s_red and TMEM free for the next chunk
+      named_sync(1, 128);  // s_red, P and the output columns free for the next chunk
     }
     // this split's partial: (max, sum) per head, unnormalised output per dim
     if (ct < 8) {

@@ -51,7 +51,7 @@ std::string cu_error_string(CUresult r) {
 
 CommConfig config_from_list(const std::vector<int64_t>& v) {
   CommConfig c;
-  auto at = [&](size_t i, int64_t d) { return i < v.size() ? v[i] : d; };
+  auto at = [&](size_t i, int64_t d) { return i < v.size() && v[i] >= 0 ? v[i] : d; };
   c.oneshot_max = at(0, c.oneshot_max);
   c.chunk_max = at(1, c.chunk_max);
   c.max_ctas = static_cast<int>(at(2, c.max_ctas));
@@ -63,6 +63,7 @@ CommConfig config_from_list(const std::vector<int64_t>& v) {
   c.hybrid_p2p_permille = static_cast<int>(at(8, c.hybrid_p2p_permille));
   c.hybrid_p2p_ctas = static_cast<int>(at(9, c.hybrid_p2p_ctas));
   c.hybrid_nvls_ctas = static_cast<int>(at(10, c.hybrid_nvls_ctas));
+  c.oneshot_grain = static_cast<int>(at(11, c.oneshot_grain));
   return c;
 }
 
@@ -105,6 +106,8 @@ Layout make_layout(int ws, const CommConfig& cfg) {
   if (cfg.max_ctas < 1 || cfg.max_ctas > kMaxBlocks || cfg.oneshot_ctas < 1 ||
       cfg.oneshot_ctas > kMaxBlocks)
     throw std::invalid_argument("CTA counts must be in [1, 160]");
+  if (cfg.oneshot_grain < 32 || cfg.oneshot_grain > (1 << 20))
+    throw std::invalid_argument("oneshot_grain must be in [32, 2^20] packs");
   if (cfg.chunk_max != 0 && (cfg.chunk_max < 16 * 512 || cfg.chunk_max % 16 != 0))
     throw std::invalid_argument("chunk_max must be 0 (auto) or a multiple of 16 and >= 8 KiB");
   if (cfg.oneshot_max % 16 != 0) throw std::invalid_argument("oneshot_max must be a multiple of 16");
@@ -342,7 +345,7 @@ LaunchPlan Communicator::plan(int64_t nbytes, int algo, bool registered, int dty
     case kAlgoOneshotPull: {
       if (algo != kAlgoOneshotPull && nbytes > cfg_.oneshot_max)
         throw std::invalid_argument("message exceeds the one-shot workspace");
-      const int64_t b = clampv<int64_t>(ceil_div_host(npacks, 1024), 1, cfg_.oneshot_ctas);
+      const int64_t b = clampv<int64_t>(ceil_div_host(npacks, cfg_.oneshot_grain), 1, cfg_.oneshot_ctas);
       pl.grid = dim3(static_cast<unsigned>(b));
       break;
     }

@@ -31,7 +31,11 @@ struct CommConfig {
   // 512 KiB / world size (a CTA moves ~512 KiB per round at any world size).
   int64_t chunk_max = 0;
   int max_ctas = 128;             // CTAs of the round-based tiled protocols
-  int oneshot_ctas = 32;          // CTAs of the one-shot protocols
+  // One-shot launch shape: a CTA per oneshot_grain packs (16 B), at most
+  // oneshot_ctas (measured on 8 B200s: 512 x 64 was at least as fast as any
+  // other shape at every size up to 1 MiB, eager and in CUDA graphs)
+  int oneshot_ctas = 64;
+  int oneshot_grain = 512;
   int64_t fused_bytes = 512 << 10;  // fused one-shot slot (allreduce + norm)
   uint64_t timeout_ns = 5000000000ull;
   int pipe_ctas = kPipeCtas;             // CTAs of the pipelined two-shot
@@ -45,7 +49,8 @@ struct CommConfig {
 
 // Config from a flat list: [oneshot_max, chunk_max, max_ctas, oneshot_ctas,
 // fused_bytes, timeout_ns, pipe_ctas, pipe_tile, hybrid_p2p_permille,
-// hybrid_p2p_ctas, hybrid_nvls_ctas]; missing entries keep defaults.
+// hybrid_p2p_ctas, hybrid_nvls_ctas, oneshot_grain]; missing or negative
+// entries keep their defaults.
 CommConfig config_from_list(const std::vector<int64_t>& v);
 
 // Protocol steps of the automatic choice for one dtype: the first step whose

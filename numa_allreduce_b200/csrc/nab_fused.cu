@@ -332,11 +332,13 @@ __global__ void __launch_bounds__(kFThreads) k_slots_rmsnorm(const char* base, i
 // blocks k hold rows [k ws, (k + 1) ws); CTA c takes blocks c, c + C, ...
 //   phase A  for the owned row of each block: wait (bounded) for every rank's
 //            tiles covering it, add the ws partials in rank order and the
-//            residual -> z (bf16); residual = z, out = norm(z); z replaces
-//            this rank's own partial of the row in its slot (published);
+//            residual -> z (bf16); residual = z, out = norm(z); z is stored
+//            into row t of slot [this rank] on every rank (a row no GEMM
+//            epilogue writes there: only the owner receives row t);
 //   exchange release this CTA's flag on every peer, acquire every peer's;
-//   phase B  for the other owners' rows of the same blocks: pull z from the
-//            owner's slot, residual = z, out = norm(z).
+//   phase B  for the other owners' rows of the same blocks: read z from this
+//            rank's own slot [owner], residual = z, out = norm(z).
+// All NVLink traffic is stores (posted writes; no load round trips).
 // Every rank computes the norm from the same bf16 z, so all hold the same
 // bits. A slot's parity is reused two calls later; by then every peer has
 // passed this call's exchange of the next call, so nobody still reads it.
@@ -406,8 +408,10 @@ __global__ void __launch_bounds__(kFThreads) k_slots_rs_rmsnorm(const __grid_con
 #pragma unroll
         for (int q = 1; q < kMaxRanks; ++q)
           if (q < ws) acc_add(acc, v[q]);
-        ss += finish_pack(acc, ld_plain(a.residual + o + idx), a.residual + o + idx, slot_row(rank, rank, t) + idx,
-                          z[kk]);
+        ss += finish_pack(acc, ld_plain(a.residual + o + idx), a.residual + o + idx, nullptr, z[kk]);
+        // publish z on every peer (staggered by rank)
+        const uint4 zb = ld_plain(a.residual + o + idx);
+        for (int j = 1; j < ws; ++j) st_plain(slot_row((rank + j) % ws, rank, t) + idx, zb);
       }
     }
     norm_store<PPT>(z, ss, a.wgt, a.out + o, hp, a.H, a.eps);
@@ -423,7 +427,7 @@ __global__ void __launch_bounds__(kFThreads) k_slots_rs_rmsnorm(const __grid_con
       const int q = peers[j];
       const int t = k * ws + q;
       if (t >= a.T) continue;
-      const uint4* src = slot_row(q, q, t);
+      const uint4* src = slot_row(rank, q, t);
       const int64_t o = static_cast<int64_t>(t) * hp;
       float z[PPT][8];
       float ss = 0.f;

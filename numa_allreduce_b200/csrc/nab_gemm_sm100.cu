@@ -527,36 +527,33 @@ int gemm_ar_mode_for(int T, int ws) {
   // One-shot: every rank's whole output crosses to every peer ((ws - 1) T H
   // elements per direction) but needs no second exchange; reduce-scatter +
   // gather moves 2 (ws - 1) / ws T H and adds one flag round trip. At two
-  // ranks both move the same bytes (measured: one-shot faster at every T);
-  // from four ranks on, the bytes win once there are a few rows per rank.
+  // ranks both move the same bytes; measured at 4 and 8 ranks (Llama-3-8B
+  // down projection) the one-shot led up to 128 tokens, so the
+  // reduce-scatter is taken only for larger outputs.
   if (ws <= 2) return kGemmArOneshot;
-  return T >= 8 * ws ? kGemmArReduceScatter : kGemmArOneshot;
+  return T >= 256 ? kGemmArReduceScatter : kGemmArOneshot;
 }
 
 int gemm_splits_for(int T, int N, int K, int sms) {
-  (void)sms;  // the device's own occupancy answer accounts for the SMs
+  if (sms <= 0) sms = sm_count();
+  // Fill every CTA slot of the device once: the largest split count with
+  // tiles x splits <= CTAs per SM x SMs, at least 8 k-blocks per split, and
+  // clusters of at most 8 CTAs when one CTA fills an SM (larger ones leave
+  // GPCs fragmented). Measured on B200 over the Llama-3-70B TP-8 projections
+  // at 1-128 tokens (bench/gemm.py --split-sweep), this is the best count or
+  // within a few percent of it, where a wave-count model missed by up to 15 %.
   const int bn = pick_bn(T);
   const int tiles = (N / kBM) * ((T + bn - 1) / bn);
   const int kb = K / kBK;
-  // Time model in k-blocks: waves of co-resident clusters x (k-blocks per
-  // split + a fixed cost per CTA for its prologue and epilogue). Ties go to
-  // fewer splits.
-  const int fixed = bn <= 32 ? 3 : 2;
-  int best = 1;
-  int64_t best_cost = INT64_MAX;
-  for (int sp = 1; sp <= kMaxSplits && sp <= kb; ++sp) {
+  const int per_sm = bn <= 32 ? 2 : 1;
+  const int cap = std::min({bn <= 32 ? kMaxSplits : 8, std::max(1, (per_sm * sms) / tiles), std::max(1, kb / 8)});
+  for (int sp = cap; sp > 1; --sp) {
     const int per = (kb + sp - 1) / sp;
     if ((kb + per - 1) / per != sp) continue;  // would leave a split without work
-    const int clusters = active_clusters(bn, sp);
-    if (clusters == 0) continue;
-    const int64_t waves = (tiles + clusters - 1) / clusters;
-    const int64_t cost = waves * (per + fixed);
-    if (cost < best_cost) {
-      best_cost = cost;
-      best = sp;
-    }
+    if (active_clusters(bn, sp) == 0) continue;
+    return sp;
   }
-  return best;
+  return 1;
 }
 
 void gemm_bf16(cudaStream_t s, const void* wt, const void* x, void* y, int T, int N, int K, int splits,

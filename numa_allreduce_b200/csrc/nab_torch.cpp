@@ -511,7 +511,7 @@ void silu_mul_op(const at::Tensor& gu, at::Tensor& out) {
 TORCH_LIBRARY(nab, m) {
   m.def("meta_size() -> int", &meta_size);
   // cfg: [oneshot_max, chunk_max, max_ctas, oneshot_ctas, fused_bytes, timeout_ns, pipe_ctas, pipe_tile,
-  //       hybrid_p2p_permille, hybrid_p2p_ctas, hybrid_nvls_ctas]
+  //       hybrid_p2p_permille, hybrid_p2p_ctas, hybrid_nvls_ctas, oneshot_grain]; negative = default
   m.def("layout(int ws, int[] cfg) -> int[]", &layout);
   m.def("init(int[] ws_ptrs, Tensor rank_data, int rank, bool full_nvlink, int[] cfg) -> int", &init);
   m.def("dispose(int fa) -> ()", &dispose);

@@ -20,7 +20,7 @@ FUSED_ALGOS = {"auto": 0, "oneshot": 1, "twoshot": 2}
 
 class EmulatedGroup:
     def __init__(self, world_size: int, device: torch.device | str = "cuda", *, oneshot_max: int = 1 << 20,
-                 chunk_max: int = 0, max_ctas: int = 128, oneshot_ctas: int = 32,
+                 chunk_max: int = 0, max_ctas: int = 128, oneshot_ctas: int = 64,
                  fused_bytes: int = 512 << 10, timeout_ns: int = 2_000_000_000,
                  groups: list[list[int]] | None = None, pipe_ctas: int = 128, pipe_tile: int = 256 << 10):
         if not 2 <= world_size <= 8:

@@ -106,7 +106,7 @@ def gemm_allreduce_rmsnorm(comm, x: torch.Tensor, wt: torch.Tensor, residual: to
     reduces the rows this rank owns, applies residual + norm, and gathers the
     other owners' new residual rows (about 2/ws of the one-shot's NVLink
     bytes, one more flag exchange). ``"auto"`` takes the reduce-scatter from
-    4 ranks and 8 rows per rank on (at 2 ranks both move the same bytes). ``splits=0`` picks the split-K factor (split partials
+    4 ranks and 256 rows on (at 2 ranks both move the same bytes). ``splits=0`` picks the split-K factor (split partials
     are added on this GPU before the tile is sent)."""
     if out is None:
         out = torch.empty_like(residual)

@@ -85,7 +85,8 @@ class NumaAwareAllReduce:
 
     def __init__(self, group, device, max_size: int | None = None, enable_optimization: bool = True, *,
                  oneshot_max: int = 1 << 20, chunk_max: int = 0, max_ctas: int = 128,
-                 oneshot_ctas: int = 32, fused_bytes: int = 512 << 10, pipe_ctas: int | None = None,
+                 oneshot_ctas: int = 64, oneshot_grain: int = -1, fused_bytes: int = 512 << 10,
+                 pipe_ctas: int | None = None,
                  pipe_tile: int | None = None,
                  hier_groups: list[list[int]] | None = None, topology: NumaTopology | None = None,
                  use_nvls: bool | None = None, timeout_ns: int | None = None,
@@ -150,7 +151,7 @@ class NumaAwareAllReduce:
         pipe_ctas = pipe_ctas if pipe_ctas is not None else self.env.pipe_ctas
         pipe_tile = pipe_tile if pipe_tile is not None else self.env.pipe_tile
         self._cfg = [oneshot_max, chunk_max, max_ctas, oneshot_ctas, fused_bytes, int(timeout), pipe_ctas,
-                     pipe_tile]
+                     pipe_tile, -1, -1, -1, oneshot_grain]
         self.fused_bytes = fused_bytes  # per-rank slot of the fused ops (GEMM + allreduce output)
         lay = ops.layout(self.world_size, self._cfg)
         self.workspace_bytes = int(lay[0])
