@@ -3,7 +3,8 @@
 
 ``y[T, N] = x[T, K] @ wt[N, K].T`` in bf16, fp32 accumulation, for the
 projections one rank runs per layer (qkv 1280x8192, o 8192x1024, gate|up
-7168x8192, down 8192x3584, lm_head 16128x8192) and token counts 1..512.
+7168x8192, down 8192x3584, lm_head 16128x8192) and token counts 1..512;
+`--shapes 8b_qkv,8b_o,8b_gate_up,8b_down` gives the Llama-3-8B TP-8 ones.
 Weights rotate over enough copies to exceed the 126 MB L2, so every call
 streams its weight from HBM; each variant is timed as `--calls` launches
 captured in one CUDA graph (launch overhead as in a decode step), CUDA
@@ -34,13 +35,16 @@ from numa_allreduce_b200.ops import _ext  # noqa: E402
 from numa_allreduce_b200.ops.gemm import gemm, pack_weight  # noqa: E402
 
 SHAPES = {"qkv": (1280, 8192), "o": (8192, 1024), "gate_up": (7168, 8192), "down": (8192, 3584),
-          "lm_head": (16128, 8192)}
+          "lm_head": (16128, 8192),
+          # Llama-3-8B at TP 8 (the fused layer tail's down projection is 8b_down)
+          "8b_qkv": (768, 4096), "8b_o": (4096, 512), "8b_gate_up": (3584, 4096), "8b_down": (4096, 1792)}
+DEFAULT_SHAPES = "qkv,o,gate_up,down,lm_head"
 
 
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--tokens", default="1,8,16,32,64,128,512")
-    p.add_argument("--shapes", default=",".join(SHAPES))
+    p.add_argument("--shapes", default=DEFAULT_SHAPES, help="comma list of " + ",".join(SHAPES))
     p.add_argument("--calls", type=int, default=20)
     p.add_argument("--reps", type=int, default=5)
     p.add_argument("--splits", type=int, default=0, help="force a split count (0: the heuristic)")

@@ -534,26 +534,97 @@ int gemm_ar_mode_for(int T, int ws) {
   return T >= 256 ? kGemmArReduceScatter : kGemmArOneshot;
 }
 
-int gemm_splits_for(int T, int N, int K, int sms) {
-  if (sms <= 0) sms = sm_count();
-  // Fill every CTA slot of the device once: the largest split count with
-  // tiles x splits <= CTAs per SM x SMs, at least 8 k-blocks per split, and
-  // clusters of at most 8 CTAs when one CTA fills an SM (larger ones leave
-  // GPCs fragmented). Measured on B200 over the Llama-3-70B TP-8 projections
-  // at 1-128 tokens (bench/gemm.py --split-sweep), this is the best count or
-  // within a few percent of it, where a wave-count model missed by up to 15 %.
-  const int bn = pick_bn(T);
-  const int tiles = (N / kBM) * ((T + bn - 1) / bn);
-  const int kb = K / kBK;
+namespace {
+
+// Split rule "waves": a time model in k-blocks, waves of co-resident
+// clusters x (k-blocks per split + a fixed cost per CTA for its prologue and
+// epilogue); ties go to fewer splits.
+int splits_waves(int bn, int tiles, int kb) {
+  const int fixed = bn <= 32 ? 3 : 2;
+  int best = 1;
+  int64_t best_cost = INT64_MAX;
+  for (int sp = 1; sp <= kMaxSplits && sp <= kb; ++sp) {
+    const int per = (kb + sp - 1) / sp;
+    if ((kb + per - 1) / per != sp) continue;  // would leave a split without work
+    const int clusters = active_clusters(bn, sp);
+    if (clusters == 0) continue;
+    const int64_t waves = (tiles + clusters - 1) / clusters;
+    const int64_t cost = waves * (per + fixed);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = sp;
+    }
+  }
+  return best;
+}
+
+// Split rule "fill": fill every CTA slot of the device once, the largest
+// split count with tiles x splits <= CTAs per SM x SMs and at least 8
+// k-blocks per split, clusters of at most 8 CTAs when one CTA fills an SM.
+// Best or within a few percent of the best for a GEMM that has the device to
+// itself (bench/gemm.py --split-sweep, Llama-3-70B TP-8 projections), but
+// slower than both other rules inside a decode step.
+int splits_fill(int bn, int tiles, int kb, int sms) {
   const int per_sm = bn <= 32 ? 2 : 1;
   const int cap = std::min({bn <= 32 ? kMaxSplits : 8, std::max(1, (per_sm * sms) / tiles), std::max(1, kb / 8)});
   for (int sp = cap; sp > 1; --sp) {
     const int per = (kb + sp - 1) / sp;
-    if ((kb + per - 1) / per != sp) continue;  // would leave a split without work
+    if ((kb + per - 1) / per != sp) continue;
     if (active_clusters(bn, sp) == 0) continue;
     return sp;
   }
   return 1;
+}
+
+// Split rule "pow2" (the default): the largest power of two with tiles x
+// splits <= CTA
+// slots of the device (2 per SM when the tile is at most 32 tokens wide, else
+// 1), at least 2 k-blocks per split, clusters of at most 16 (8 when one CTA
+// fills an SM). A cluster of 5-7 CTAs at one CTA per SM packs badly into
+// the GPCs (Llama-3-8B gate|up at 64 tokens: 12.0 us at 4 splits, 20.3 us at
+// 5). Within 8 % of the best count on every Llama-3-8B / 70B TP-8 projection
+// at 1-128 tokens measured alone on the device, and the fastest of the three
+// rules inside the Llama-3-70B TP-8 decode step (one GPU's shard, CUDA graph:
+// 5.19 / 6.35 ms per token at batch 1 / 32 against 5.71 / 6.53 for "waves"
+// and 6.07 / 6.76 for "fill").
+int splits_pow2(int bn, int tiles, int kb, int sms) {
+  const int per_sm = bn <= 32 ? 2 : 1;
+  const int cap = std::min({bn <= 32 ? kMaxSplits : 8, std::max(1, (per_sm * sms) / tiles), std::max(1, kb / 2)});
+  int sp = 1;
+  while (sp * 2 <= cap) sp *= 2;
+  for (; sp > 1; sp /= 2) {
+    const int per = (kb + sp - 1) / sp;
+    if ((kb + per - 1) / per != sp) continue;
+    if (active_clusters(bn, sp) == 0) continue;
+    return sp;
+  }
+  return 1;
+}
+
+enum SplitRule { kSplitWaves, kSplitFill, kSplitPow2 };
+
+SplitRule split_rule() {
+  static const SplitRule rule = [] {
+    const char* v = std::getenv("NAB_GEMM_SPLIT_RULE");
+    if (v != nullptr && std::strcmp(v, "fill") == 0) return kSplitFill;
+    if (v != nullptr && std::strcmp(v, "waves") == 0) return kSplitWaves;
+    return kSplitPow2;
+  }();
+  return rule;
+}
+
+}  // namespace
+
+int gemm_splits_for(int T, int N, int K, int sms) {
+  if (sms <= 0) sms = sm_count();
+  const int bn = pick_bn(T);
+  const int tiles = (N / kBM) * ((T + bn - 1) / bn);
+  const int kb = K / kBK;
+  switch (split_rule()) {
+    case kSplitFill: return splits_fill(bn, tiles, kb, sms);
+    case kSplitWaves: return splits_waves(bn, tiles, kb);
+    default: return splits_pow2(bn, tiles, kb, sms);  // kSplitPow2
+  }
 }
 
 void gemm_bf16(cudaStream_t s, const void* wt, const void* x, void* y, int T, int N, int K, int splits,

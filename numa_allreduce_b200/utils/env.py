@@ -26,6 +26,9 @@ reads. Every variable below is actually read:
                            P2P share of the message and each part's CTAs
 ``NAB_GEMM_PDL``           ``0`` launches the GEMMs without programmatic
                            dependent launch (read by the native code)
+``NAB_GEMM_SPLIT_RULE``    split-K count: ``pow2`` (default, the largest
+                           power of two that fits the CTA slots), ``waves``
+                           (a wave-count model) or ``fill`` (every slot)
 ``NAB_NO_BUILD``           ``1``: never compile the extension on import
 =========================  ===================================================
 """
