@@ -5,11 +5,15 @@ Public API (parity with the reference's ``src/__init__.py``, which exported
 
 * :class:`NumaAwareAllReduce`: custom allreduce over NVLink 5 / NVSwitch with
   one-shot, two-shot, NVLink SHARP and hierarchical (NUMA-grouped) protocols,
-  CUDA-graph buffer registration and bounded device waits;
+  CUDA-graph buffer registration and bounded device waits, plus
+  ``reduce_scatter`` / ``all_gather`` over contiguous rank segments;
 * :class:`NumaTopology`, :class:`NumaNodeInfo`, :class:`GpuNumaInfo`,
   :func:`detect_numa_topology`: NUMA and GPU topology detection;
 * :class:`HierSchedule` and :func:`emulate_allreduce`: the schedule and its
-  gloo/CPU executor;
+  gloo/CPU executor (:func:`emulate_reduce_scatter`, :func:`emulate_all_gather`
+  for the segment collectives; :func:`reference_allreduce`,
+  :func:`reference_reduce_scatter`, :func:`reference_all_gather`: exact CPU
+  oracles);
 * :func:`fused_allreduce_rmsnorm`, :func:`rmsnorm_residual`: the fused TP
   layer tail;
 * :func:`gemm`, :func:`gemm_swiglu`, :func:`gemm_allreduce_rmsnorm`,
@@ -27,9 +31,9 @@ from .ops.errors import KernelError, check_kernels, reset_kernels
 from .ops.fused import fused_allreduce_rmsnorm, rmsnorm_residual
 from .ops.gemm import PackedWeight, gemm, gemm_allreduce_rmsnorm, gemm_swiglu, interleave_gate_up, pack_weight
 from .parallel.comm import AllReduceError, NumaAwareAllReduce
-from .parallel.emulate import emulate_allreduce
+from .parallel.emulate import emulate_all_gather, emulate_allreduce, emulate_reduce_scatter
 from .parallel.health import PeerLost, PeerMonitor
-from .parallel.schedule import HierSchedule, reference_allreduce
+from .parallel.schedule import HierSchedule, reference_all_gather, reference_allreduce, reference_reduce_scatter
 from .parallel.select import AlgoSelector
 from .utils.topology import GpuNumaInfo, NumaNodeInfo, NumaTopology, detect_numa_topology
 
@@ -47,14 +51,18 @@ __all__ = [
     "PeerMonitor",
     "check_kernels",
     "detect_numa_topology",
+    "emulate_all_gather",
     "emulate_allreduce",
+    "emulate_reduce_scatter",
     "fused_allreduce_rmsnorm",
     "gemm",
     "gemm_allreduce_rmsnorm",
     "gemm_swiglu",
     "interleave_gate_up",
     "pack_weight",
+    "reference_all_gather",
     "reference_allreduce",
+    "reference_reduce_scatter",
     "reset_kernels",
     "rmsnorm_residual",
 ]

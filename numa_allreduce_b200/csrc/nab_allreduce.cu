@@ -661,6 +661,167 @@ __global__ void __launch_bounds__(kThreads) k_oneshot_pull(const __grid_constant
   end_call(me, epoch);
 }
 
+// ------------------------------------------ reduce-scatter / all-gather ----
+// Contiguous-segment collectives, one launch per piece of at most
+// oneshot_max bytes per segment (the host walks longer segments piece by
+// piece). Both use the one-shot slots, double buffered by call parity: a rank
+// can only start call e + 2 after every peer has arrived at call e + 1, which
+// each does after its call e has finished reading, so no end barrier.
+//   reduce-scatter: the input holds WS segments seg_stride packs apart; rank
+//     r pushes segment j into slot [r] of rank j, then sums its own segment
+//     over the WS contributions in rank order (fp32, one rounding).
+//   all-gather: rank r pushes its input into slot [r] of every peer, then
+//     copies the WS segments (its own from the input) into the output,
+//     seg_stride packs apart.
+// Capability parity: the reduce-scatter and all-gather stages of the
+// reference's dead three-stage path (src/numa_all_reduce.cu:228-268, 318-344),
+// here as standalone collectives over all ranks.
+template <typename T, int WS>
+__global__ void __launch_bounds__(kThreads, 1) k_reduce_scatter(const __grid_constant__ ARParams p) {
+  constexpr int UP = Unroll<WS>::kPeer;
+  constexpr int UR = Unroll<WS>::kRed;
+  const RankView& me = p.v[blockIdx.y];
+  if (!launch_ok(p, me, WS, p.npacks * 16 <= p.L.oneshot_max && p.seg_stride >= p.npacks &&
+                                p.L.oneshot_off + 2 * WS * p.L.oneshot_max <= p.L.ws_bytes))
+    return;
+  const int rank = me.rank;
+  const uint32_t epoch = begin_call(me);
+  const WaitCtx w = make_wait(p, me, epoch);
+  const int parity = epoch & 1;
+  const int64_t per = ceil_div<int64_t>(p.npacks, gridDim.x);
+  const int64_t beg = per * blockIdx.x;
+  const int64_t end = min(p.npacks, beg + per);
+  const uint4* src = reinterpret_cast<const uint4*>(me.in);
+  const int64_t stride = p.seg_stride;
+  const int64_t slot_packs = p.L.oneshot_max / 16;
+  auto slot = [&](int owner_rank, int src_rank) -> uint4* {
+    return reinterpret_cast<uint4*>(me.wsp[owner_rank] + p.L.oneshot_off) +
+           (static_cast<int64_t>(parity) * WS + src_rank) * slot_packs;
+  };
+  // 1. segment j of my input -> slot [rank] of rank j
+  for (int64_t i0 = beg + threadIdx.x; i0 < end; i0 += static_cast<int64_t>(blockDim.x) * UP) {
+    uint4 x[UP][WS - 1];
+#pragma unroll
+    for (int u = 0; u < UP; ++u) {
+      const int64_t i = i0 + static_cast<int64_t>(u) * blockDim.x;
+      if (i < end) {
+#pragma unroll
+        for (int k = 1; k < WS; ++k) x[u][k - 1] = ld_plain(src + ((rank + k) % WS) * stride + i);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < UP; ++u) {
+      const int64_t i = i0 + static_cast<int64_t>(u) * blockDim.x;
+      if (i < end && NAB_DBG_IDX(i, slot_packs)) {
+#pragma unroll
+        for (int k = 1; k < WS; ++k) st_plain(slot((rank + k) % WS, rank) + i, x[u][k - 1]);
+      }
+    }
+  }
+  int peers[WS - 1];
+  all_peers<WS>(rank, peers);
+  const bool ok = exchange(me, kFlagScatter, blockIdx.x, make_seq(epoch, 0), peers, WS - 1, w,
+                           kStageReduceScatter);
+  // 2. my segment: the WS contributions in rank order
+  if (ok) {
+    uint4* dst = reinterpret_cast<uint4*>(me.out);
+    const uint4* own = src + rank * stride;
+    for (int64_t i0 = beg + threadIdx.x; i0 < end; i0 += static_cast<int64_t>(blockDim.x) * UR) {
+      uint4 x[UR][WS];
+#pragma unroll
+      for (int u = 0; u < UR; ++u) {
+        const int64_t i = i0 + static_cast<int64_t>(u) * blockDim.x;
+        if (i < end) {
+#pragma unroll
+          for (int q = 0; q < WS; ++q) x[u][q] = (q == rank) ? ld_plain(own + i) : ld_cg(slot(rank, q) + i);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < UR; ++u) {
+        const int64_t i = i0 + static_cast<int64_t>(u) * blockDim.x;
+        if (i < end) {
+          Acc<T> a;
+          acc_set(a, x[u][0]);
+#pragma unroll
+          for (int q = 1; q < WS; ++q) acc_add(a, x[u][q]);
+          st_plain(dst + i, acc_pack(a));
+        }
+      }
+    }
+  }
+  end_call(me, epoch);
+}
+
+template <int WS>
+__global__ void __launch_bounds__(kThreads, 1) k_all_gather(const __grid_constant__ ARParams p) {
+  constexpr int U = 4;
+  constexpr int UR = Unroll<WS>::kRed;
+  const RankView& me = p.v[blockIdx.y];
+  if (!launch_ok(p, me, WS, p.npacks * 16 <= p.L.oneshot_max && p.seg_stride >= p.npacks &&
+                                p.L.oneshot_off + 2 * WS * p.L.oneshot_max <= p.L.ws_bytes))
+    return;
+  const int rank = me.rank;
+  const uint32_t epoch = begin_call(me);
+  const WaitCtx w = make_wait(p, me, epoch);
+  const int parity = epoch & 1;
+  const int64_t per = ceil_div<int64_t>(p.npacks, gridDim.x);
+  const int64_t beg = per * blockIdx.x;
+  const int64_t end = min(p.npacks, beg + per);
+  const uint4* src = reinterpret_cast<const uint4*>(me.in);
+  const int64_t stride = p.seg_stride;
+  const int64_t slot_packs = p.L.oneshot_max / 16;
+  auto slot = [&](int owner_rank, int src_rank) -> uint4* {
+    return reinterpret_cast<uint4*>(me.wsp[owner_rank] + p.L.oneshot_off) +
+           (static_cast<int64_t>(parity) * WS + src_rank) * slot_packs;
+  };
+  uint4* dst = reinterpret_cast<uint4*>(me.out);
+  // 1. my input -> slot [rank] of every peer, and -> my own output segment
+  for (int64_t i0 = beg + threadIdx.x; i0 < end; i0 += static_cast<int64_t>(blockDim.x) * U) {
+    uint4 x[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t i = i0 + static_cast<int64_t>(u) * blockDim.x;
+      if (i < end) x[u] = ld_plain(src + i);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t i = i0 + static_cast<int64_t>(u) * blockDim.x;
+      if (i < end && NAB_DBG_IDX(i, slot_packs)) {
+#pragma unroll
+        for (int k = 1; k < WS; ++k) st_plain(slot((rank + k) % WS, rank) + i, x[u]);
+        st_plain(dst + rank * stride + i, x[u]);
+      }
+    }
+  }
+  int peers[WS - 1];
+  all_peers<WS>(rank, peers);
+  const bool ok = exchange(me, kFlagGather, blockIdx.x, make_seq(epoch, 0), peers, WS - 1, w,
+                           kStageAllGather);
+  // 2. the peers' segments from my slots into the output
+  if (ok) {
+    for (int64_t i0 = beg + threadIdx.x; i0 < end; i0 += static_cast<int64_t>(blockDim.x) * UR) {
+      uint4 x[UR][WS - 1];
+#pragma unroll
+      for (int u = 0; u < UR; ++u) {
+        const int64_t i = i0 + static_cast<int64_t>(u) * blockDim.x;
+        if (i < end) {
+#pragma unroll
+          for (int k = 1; k < WS; ++k) x[u][k - 1] = ld_cg(slot(rank, (rank + k) % WS) + i);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < UR; ++u) {
+        const int64_t i = i0 + static_cast<int64_t>(u) * blockDim.x;
+        if (i < end) {
+#pragma unroll
+          for (int k = 1; k < WS; ++k) st_plain(dst + ((rank + k) % WS) * stride + i, x[u][k - 1]);
+        }
+      }
+    }
+  }
+  end_call(me, epoch);
+}
+
 // ---------------------------------------------------------- NVLS oneshot ----
 template <typename T, int WS>
 __global__ void __launch_bounds__(kThreads, 2) k_nvls_oneshot(const __grid_constant__ ARParams p) {
@@ -945,6 +1106,8 @@ cudaError_t launch_ws(int algo, const ARParams& p, dim3 grid, cudaStream_t s, bo
     case kAlgoNvlsOneshot: fn = reinterpret_cast<void*>(&k_nvls_oneshot<T, WS>); break;
     case kAlgoNvlsTwoshot: fn = reinterpret_cast<void*>(&k_nvls_twoshot<T, WS>); break;
     case kAlgoHybrid: fn = reinterpret_cast<void*>(&k_hybrid<T, WS>); break;
+    case kAlgoReduceScatter: fn = reinterpret_cast<void*>(&k_reduce_scatter<T, WS>); break;
+    case kAlgoAllGather: fn = reinterpret_cast<void*>(&k_all_gather<WS>); break;
     default: return cudaErrorInvalidValue;
   }
   void* args[] = {const_cast<ARParams*>(&p)};

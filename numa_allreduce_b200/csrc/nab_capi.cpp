@@ -119,6 +119,26 @@ NAB_API int nab_allreduce(void* ptr, cudaStream_t stream, const void* input, voi
   return do_allreduce(ptr, stream, input, output, numel, dtype, algo);
 }
 
+// Contiguous-segment collectives; seg_numel elements per rank segment.
+// Reduce-scatter: input holds world_size segments, output one (the sum of
+// every rank's segment [rank]). All-gather: input one segment, output
+// world_size (rank order).
+NAB_API int nab_reduce_scatter(void* ptr, cudaStream_t stream, const void* input, void* output, int64_t seg_numel,
+                               int dtype) {
+  return guarded([&] {
+    if (!ptr) throw std::invalid_argument("null communicator");
+    C(ptr)->reduce_scatter(stream, input, output, seg_numel * (dtype == nab::kF32 ? 4 : 2), dtype);
+  });
+}
+
+NAB_API int nab_all_gather(void* ptr, cudaStream_t stream, const void* input, void* output, int64_t seg_numel,
+                           int dtype) {
+  return guarded([&] {
+    if (!ptr) throw std::invalid_argument("null communicator");
+    C(ptr)->all_gather(stream, input, output, seg_numel * (dtype == nab::kF32 ? 4 : 2), dtype);
+  });
+}
+
 // Replaces the automatic choice's steps for one dtype (0 fp32, 1 fp16, 2
 // bf16): n ascending byte limits with their protocol ids, and the protocol of
 // larger messages (100 = NCCL, which this ABI cannot call: such messages take

@@ -478,6 +478,84 @@ int Communicator::allreduce(cudaStream_t s, const void* in, void* out, int64_t n
   return pl.algo;
 }
 
+dim3 Communicator::collective_grid(int64_t piece_bytes) const {
+  const int64_t b = clampv<int64_t>(ceil_div_host(piece_bytes / 16, cfg_.oneshot_grain), 1, cfg_.max_ctas);
+  return dim3(static_cast<unsigned>(b));
+}
+
+namespace {
+
+void check_collective_args(const void* in, const void* out, int64_t seg_bytes, int dtype) {
+  if (seg_bytes <= 0 || seg_bytes % 16 != 0)
+    throw std::invalid_argument("segment size must be a positive multiple of 16 bytes");
+  if (dtype != kF32 && dtype != kF16 && dtype != kBF16)
+    throw std::invalid_argument("collectives support float32, float16 and bfloat16");
+  if (reinterpret_cast<uintptr_t>(in) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
+    throw std::invalid_argument("collective buffers must be 16-byte aligned");
+  if (in == out) throw std::invalid_argument("collectives need distinct input and output buffers");
+}
+
+// Byte offsets of piece k in the segmented buffer (reduce-scatter input /
+// all-gather output) and in the one-segment buffer.
+struct Piece {
+  int64_t off;    // into every segment
+  int64_t bytes;  // this piece
+};
+
+std::vector<Piece> pieces_of(int64_t seg_bytes, int64_t cap) {
+  std::vector<Piece> v;
+  for (int64_t off = 0; off < seg_bytes; off += cap) v.push_back({off, std::min(cap, seg_bytes - off)});
+  return v;
+}
+
+}  // namespace
+
+int Communicator::reduce_scatter(cudaStream_t s, const void* in, void* out, int64_t seg_bytes, int dtype) {
+  check_collective_args(in, out, seg_bytes, dtype);
+  const char* src = static_cast<const char*>(in);
+  char* dst = static_cast<char*>(out);
+  int n = 0;
+  for (const Piece& pc : pieces_of(seg_bytes, cfg_.oneshot_max)) {
+    ARParams p{};
+    LaunchPlan pl;
+    pl.algo = ws_ == 1 ? kAlgoCopy : kAlgoReduceScatter;
+    pl.grid = ws_ == 1 ? dim3(static_cast<unsigned>(clampv<int64_t>(ceil_div_host(pc.bytes / 16, 4 * 512), 1, 148)))
+                       : collective_grid(pc.bytes);
+    fill_params(p, pl, pc.bytes);
+    p.seg_stride = seg_bytes / 16;
+    p.v[0] = view(src + pc.off, dst + pc.off, nullptr);
+    const cudaError_t e = launch_allreduce(pl.algo, dtype, p, pl.grid, s, false);
+    if (e != cudaSuccess)
+      throw std::runtime_error(std::string("reduce-scatter launch failed: ") + cudaGetErrorString(e));
+    count_launch();
+    ++n;
+  }
+  return n;
+}
+
+int Communicator::all_gather(cudaStream_t s, const void* in, void* out, int64_t seg_bytes, int dtype) {
+  check_collective_args(in, out, seg_bytes, dtype);
+  const char* src = static_cast<const char*>(in);
+  char* dst = static_cast<char*>(out);
+  int n = 0;
+  for (const Piece& pc : pieces_of(seg_bytes, cfg_.oneshot_max)) {
+    ARParams p{};
+    LaunchPlan pl;
+    pl.algo = ws_ == 1 ? kAlgoCopy : kAlgoAllGather;
+    pl.grid = ws_ == 1 ? dim3(static_cast<unsigned>(clampv<int64_t>(ceil_div_host(pc.bytes / 16, 4 * 512), 1, 148)))
+                       : collective_grid(pc.bytes);
+    fill_params(p, pl, pc.bytes);
+    p.seg_stride = seg_bytes / 16;
+    p.v[0] = view(src + pc.off, dst + pc.off, nullptr);
+    const cudaError_t e = launch_allreduce(pl.algo, dtype, p, pl.grid, s, false);
+    if (e != cudaSuccess)
+      throw std::runtime_error(std::string("all-gather launch failed: ") + cudaGetErrorString(e));
+    count_launch();
+    ++n;
+  }
+  return n;
+}
+
 uint32_t Communicator::error_code() const {
   return *reinterpret_cast<volatile uint32_t*>(err_host_);
 }
@@ -557,6 +635,48 @@ int emulate_allreduce(const std::vector<Communicator*>& comms, cudaStream_t s,
                       const std::vector<const void*>& ins, const std::vector<void*>& outs,
                       int64_t nbytes, int dtype, int algo, int participants) {
   return emulate_impl(comms, s, ins, outs, nbytes, dtype, algo, participants, false);
+}
+
+int emulate_collective(const std::vector<Communicator*>& comms, cudaStream_t s,
+                       const std::vector<const void*>& ins, const std::vector<void*>& outs,
+                       int64_t seg_bytes, int dtype, int kind, int participants) {
+  const int ws = static_cast<int>(comms.size());
+  if (participants < 0) participants = ws;
+  if (participants < 1 || participants > ws) throw std::invalid_argument("bad participant count");
+  if (ws < 2 || ws > kMaxRanks || static_cast<int>(ins.size()) != ws || static_cast<int>(outs.size()) != ws)
+    throw std::invalid_argument("emulation needs 2..8 communicators and one buffer per rank");
+  if (kind != kAlgoReduceScatter && kind != kAlgoAllGather)
+    throw std::invalid_argument("emulated collective must be reduce-scatter or all-gather");
+  for (int r = 0; r < ws; ++r) {
+    check_collective_args(ins[r], outs[r], seg_bytes, dtype);
+    if (comms[r]->rank() != r) throw std::invalid_argument("communicators must be in rank order");
+  }
+  Communicator* c0 = comms[0];
+  // every CTA of every emulated rank resident at once (cooperative launch)
+  int dev = 0, sms = 0;
+  NAB_CUDA_CHECK(cudaGetDevice(&dev));
+  NAB_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const unsigned cap = static_cast<unsigned>(std::max(1, sms / ws));
+  int n = 0;
+  for (const Piece& pc : pieces_of(seg_bytes, c0->config().oneshot_max)) {
+    LaunchPlan pl;
+    pl.algo = kind;
+    pl.grid = c0->collective_grid(pc.bytes);
+    pl.grid.x = std::min(pl.grid.x, cap);
+    ARParams p{};
+    c0->fill_params(p, pl, pc.bytes);
+    p.seg_stride = seg_bytes / 16;
+    for (int r = 0; r < ws; ++r)
+      p.v[r] = comms[r]->view(static_cast<const char*>(ins[r]) + pc.off, static_cast<char*>(outs[r]) + pc.off,
+                              nullptr);
+    pl.grid.y = participants;
+    const cudaError_t e = launch_allreduce(kind, dtype, p, pl.grid, s, true);
+    if (e != cudaSuccess)
+      throw std::runtime_error(std::string("emulated collective launch failed: ") + cudaGetErrorString(e));
+    for (int r = 0; r < participants; ++r) comms[r]->count_launch();
+    ++n;
+  }
+  return n;
 }
 
 #if NAB_DEBUG_BOUNDS

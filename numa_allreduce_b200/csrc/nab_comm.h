@@ -140,6 +140,16 @@ class Communicator {
   int allreduce(cudaStream_t s, const void* in, void* out, int64_t nbytes, int dtype, int algo,
                 bool registered);
 
+  // Contiguous-segment collectives; seg_bytes is one rank's segment (a
+  // positive multiple of 16). reduce_scatter: in holds ws segments, out gets
+  // the sum of every rank's segment [rank]. all_gather: in is one segment,
+  // out gets the ws ranks' segments in rank order. One launch per piece of at
+  // most oneshot_max bytes per segment; returns the number of launches.
+  int reduce_scatter(cudaStream_t s, const void* in, void* out, int64_t seg_bytes, int dtype);
+  int all_gather(cudaStream_t s, const void* in, void* out, int64_t seg_bytes, int dtype);
+  // Launch shape of one piece of those collectives (grid.x CTAs).
+  dim3 collective_grid(int64_t piece_bytes) const;
+
   // Error state written by bounded waits.
   uint32_t error_code() const;  // from host-mapped memory, no sync
   ErrorState error_state() const;  // synchronous copy of the full record
@@ -194,6 +204,13 @@ class Communicator {
 int emulate_allreduce(const std::vector<Communicator*>& comms, cudaStream_t s,
                       const std::vector<const void*>& ins, const std::vector<void*>& outs,
                       int64_t nbytes, int dtype, int algo, int participants = -1);
+
+// The reduce-scatter (kAlgoReduceScatter) or all-gather (kAlgoAllGather)
+// collective over ws emulated ranks on the current GPU, piece by piece like
+// Communicator::reduce_scatter / all_gather. Returns the number of launches.
+int emulate_collective(const std::vector<Communicator*>& comms, cudaStream_t s,
+                       const std::vector<const void*>& ins, const std::vector<void*>& outs,
+                       int64_t seg_bytes, int dtype, int kind, int participants = -1);
 
 #if NAB_DEBUG_BOUNDS
 // Debug builds only: the same launch with emulated rank 0's view claiming an

@@ -34,6 +34,10 @@ enum Algo : int {
   kAlgoTwoshotPipe = 8,  // two-shot, warp-specialised and pipelined over a slot ring
   kAlgoHybrid = 9,       // one launch: P2P pipelined two-shot on a prefix, NVLS two-shot on the rest
   kAlgoCount = 10,
+  // Not allreduce protocols (never in a tuning table): the contiguous-segment
+  // reduce-scatter and all-gather collectives on the one-shot slots.
+  kAlgoReduceScatter = 20,
+  kAlgoAllGather = 21,
   kAlgoNccl = 100,       // selector result only: the caller should use NCCL
 };
 
@@ -59,6 +63,8 @@ enum Stage : uint32_t {
   kStageGemm = 11,       // plain GEMM: its own TMA / tensor-core mbarriers
   kStageAttn = 12,       // decode attention: its own bulk-copy mbarriers
   kStageBounds = 13,     // debug builds: an index failed a bounds check
+  kStageReduceScatter = 14,
+  kStageAllGather = 15,
 };
 
 // Lives in host-mapped pinned memory so the host can read it at any time, even
@@ -96,6 +102,8 @@ enum FlagKind : int {
   kFlagFusedAG,
   kFlagPipeRS,  // pipelined two-shot: tiles pushed to this rank, per CTA
   kFlagPipeAG,  // pipelined two-shot: tiles reduced by the owner, per CTA
+  kFlagScatter, // reduce-scatter collective: segments pushed to their owners
+  kFlagGather,  // all-gather collective: this rank's segment pushed to every peer
   kFlagCount,
 };
 

@@ -64,6 +64,7 @@ struct ARParams {
   int chunk_packs2;      // hybrid: packs per owner chunk of the NVLS part
   int pad3_;
   int64_t split_packs;   // hybrid: packs [0, split_packs) go P2P, the rest NVLS
+  int64_t seg_stride;    // reduce-scatter input / all-gather output: packs between rank segments
   int8_t group_of[kMaxRanks];
   int8_t lidx_of[kMaxRanks];
   int8_t member[kMaxRanks][kMaxRanks];  // [group][local index] -> rank

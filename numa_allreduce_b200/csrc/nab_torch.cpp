@@ -123,6 +123,56 @@ void all_reduce_algo(fptr_t fa, const at::Tensor& inp, at::Tensor& out, int64_t 
                    dtype_of(inp), static_cast<int>(algo), registered);
 }
 
+// Reduce-scatter / all-gather: `big` holds ws segments of `small`'s size.
+void check_collective_io(const at::Tensor& small, const at::Tensor& big, int ws) {
+  TORCH_CHECK(small.is_cuda() && big.is_cuda(), "collective tensors must be on a CUDA device");
+  TORCH_CHECK(small.scalar_type() == big.scalar_type(), "input and output dtypes differ");
+  TORCH_CHECK(big.numel() == small.numel() * ws, "the segmented tensor must hold world_size segments");
+  TORCH_CHECK(small.is_contiguous() && big.is_contiguous(), "collective tensors must be contiguous");
+}
+
+void reduce_scatter(fptr_t fa, const at::Tensor& inp, at::Tensor& out) {
+  check_collective_io(out, inp, C(fa)->world_size());
+  const at::cuda::OptionalCUDAGuard guard(inp.device());
+  auto stream = at::cuda::getCurrentCUDAStream().stream();
+  C(fa)->reduce_scatter(stream, inp.data_ptr(), out.data_ptr(), out.numel() * out.element_size(), dtype_of(inp));
+}
+
+void all_gather(fptr_t fa, const at::Tensor& inp, at::Tensor& out) {
+  check_collective_io(inp, out, C(fa)->world_size());
+  const at::cuda::OptionalCUDAGuard guard(inp.device());
+  auto stream = at::cuda::getCurrentCUDAStream().stream();
+  C(fa)->all_gather(stream, inp.data_ptr(), out.data_ptr(), inp.numel() * inp.element_size(), dtype_of(inp));
+}
+
+// kind: 0 reduce-scatter (ins segmented, outs one segment), 1 all-gather.
+int64_t emulate_collective(const std::vector<int64_t>& fas, const std::vector<at::Tensor>& ins,
+                           const std::vector<at::Tensor>& outs, int64_t kind, int64_t participants) {
+  TORCH_CHECK(fas.size() == ins.size() && ins.size() == outs.size(), "one tensor pair per rank");
+  TORCH_CHECK(kind == 0 || kind == 1, "kind is 0 (reduce-scatter) or 1 (all-gather)");
+  const int ws = static_cast<int>(fas.size());
+  std::vector<Communicator*> cs;
+  std::vector<const void*> in_ptrs;
+  std::vector<void*> out_ptrs;
+  for (size_t i = 0; i < fas.size(); ++i) {
+    if (kind == 0)
+      check_collective_io(outs[i], ins[i], ws);
+    else
+      check_collective_io(ins[i], outs[i], ws);
+    TORCH_CHECK(ins[i].numel() == ins[0].numel() && ins[i].scalar_type() == ins[0].scalar_type(),
+                "all ranks must use the same shape and dtype");
+    cs.push_back(C(fas[i]));
+    in_ptrs.push_back(ins[i].data_ptr());
+    out_ptrs.push_back(outs[i].data_ptr());
+  }
+  const at::Tensor& seg = kind == 0 ? outs[0] : ins[0];
+  const at::cuda::OptionalCUDAGuard guard(ins[0].device());
+  auto stream = at::cuda::getCurrentCUDAStream().stream();
+  return nab::emulate_collective(cs, stream, in_ptrs, out_ptrs, seg.numel() * seg.element_size(), dtype_of(seg),
+                                 kind == 0 ? nab::kAlgoReduceScatter : nab::kAlgoAllGather,
+                                 static_cast<int>(participants));
+}
+
 int64_t plan_algo(fptr_t fa, int64_t nbytes, int64_t algo, bool registered, int64_t dtype) {
   if (C(fa)->world_size() == 1) return nab::kAlgoCopy;
   return C(fa)->plan(nbytes, static_cast<int>(algo), registered, static_cast<int>(dtype)).algo;
@@ -522,6 +572,12 @@ TORCH_LIBRARY(nab, m) {
   m.impl("all_reduce", c10::kCUDA, &all_reduce);
   m.def("all_reduce_algo(int fa, Tensor inp, Tensor(a!) out, int algo, bool registered) -> ()");
   m.impl("all_reduce_algo", c10::kCUDA, &all_reduce_algo);
+  m.def("reduce_scatter(int fa, Tensor inp, Tensor(a!) out) -> ()");
+  m.impl("reduce_scatter", c10::kCUDA, &reduce_scatter);
+  m.def("all_gather(int fa, Tensor inp, Tensor(a!) out) -> ()");
+  m.impl("all_gather", c10::kCUDA, &all_gather);
+  m.def("emulate_collective(int[] fas, Tensor[] ins, Tensor(a!)[] outs, int kind, int participants=-1) -> int");
+  m.impl("emulate_collective", c10::kCUDA, &emulate_collective);
   m.def("plan_algo(int fa, int nbytes, int algo, bool registered, int dtype=2) -> int", &plan_algo);
   m.def("plan(int fa, int nbytes, int algo, bool registered, int dtype=2) -> int[]", &plan);
   m.def("set_auto_table(int fa, int dtype, int[] limits, int[] algos, int fallback) -> ()", &set_auto_table);

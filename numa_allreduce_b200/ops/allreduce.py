@@ -48,6 +48,23 @@ class EmulatedGroup:
         self.ops.emulate_all_reduce(self.fas, inputs, outs, ALGO_IDS[algo], participants)
         return outs
 
+    def reduce_scatter(self, inputs: list[torch.Tensor], outs: list[torch.Tensor] | None = None,
+                       participants: int = -1) -> list[torch.Tensor]:
+        """Emulated reduce-scatter: ``outs[r]`` = sum over ranks of segment r
+        of ``inputs[q]`` (each input holds ``world_size`` equal segments)."""
+        n = inputs[0].numel() // self.world_size
+        outs = outs if outs is not None else [torch.empty(n, dtype=x.dtype, device=x.device) for x in inputs]
+        self.ops.emulate_collective(self.fas, inputs, outs, 0, participants)
+        return outs
+
+    def all_gather(self, inputs: list[torch.Tensor], outs: list[torch.Tensor] | None = None,
+                   participants: int = -1) -> list[torch.Tensor]:
+        """Emulated all-gather: every ``outs[r]`` = the inputs in rank order."""
+        n = inputs[0].numel() * self.world_size
+        outs = outs if outs is not None else [torch.empty(n, dtype=x.dtype, device=x.device) for x in inputs]
+        self.ops.emulate_collective(self.fas, inputs, outs, 1, participants)
+        return outs
+
     def fused_ar_rmsnorm(self, inputs, residuals, weights, eps: float = 1e-5, algo: str = "auto",
                          outs=None):
         outs = outs if outs is not None else [torch.empty_like(x) for x in inputs]

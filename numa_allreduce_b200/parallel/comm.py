@@ -23,6 +23,9 @@ Deliberate differences:
   NVLink SHARP protocols when the GPUs support multicast.
 * Every device wait is bounded; ``check()`` raises with the failing rank,
   peer and stage, and ``reset()`` re-synchronises all ranks.
+* ``reduce_scatter`` and ``all_gather`` over contiguous rank segments, the
+  stages of the reference's (dead) three-stage path
+  (src/numa_all_reduce.cu:228-268, 318-344) as collectives of their own.
 """
 
 from __future__ import annotations
@@ -44,7 +47,7 @@ logger = get_logger(__name__)
 
 STAGES = {1: "oneshot", 2: "reduce-scatter", 3: "all-gather", 4: "hier stage 2", 5: "pull start",
           6: "pull end", 7: "nvls arrive 1", 8: "nvls arrive 2", 9: "fused", 10: "gemm-allreduce",
-          13: "bounds check"}
+          13: "bounds check", 14: "reduce-scatter collective", 15: "all-gather collective"}
 
 
 class AllReduceError(RuntimeError):
@@ -384,6 +387,46 @@ class NumaAwareAllReduce:
         self._ops.all_reduce_algo(self._ptr, inp, out, ALGO_IDS[name], registered)
         if self.env.nvtx:
             torch.cuda.nvtx.range_pop()
+        if self.env.check:
+            torch.cuda.current_stream().synchronize()
+            self.check()
+        return out
+
+    def _check_collective(self, small: torch.Tensor, big: torch.Tensor) -> None:
+        if self.disabled:
+            raise RuntimeError("custom collectives are disabled")
+        if small.dtype not in (torch.float32, torch.float16, torch.bfloat16) or big.dtype != small.dtype:
+            raise ValueError("collectives take float32, float16 or bfloat16 tensors of one dtype")
+        if not (small.is_contiguous() and big.is_contiguous()):
+            raise ValueError("collective tensors must be contiguous")
+        if big.numel() != small.numel() * self.world_size:
+            raise ValueError(f"the segmented tensor must hold world_size ({self.world_size}) segments "
+                             f"of {small.numel()} elements, got {big.numel()}")
+        if small.numel() == 0 or (small.numel() * small.element_size()) % 16 != 0:
+            raise ValueError("a rank's segment must be a positive multiple of 16 bytes")
+
+    def reduce_scatter(self, inp: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """``out`` = the sum over ranks of segment ``rank`` of ``inp``.
+
+        ``inp`` holds ``world_size`` contiguous equal segments (flattened;
+        shape ``[world_size * n, ...]`` works); ``out`` gets one segment.
+        fp32 accumulation in rank order, bit-identical to the matching slice
+        of :meth:`all_reduce`'s result."""
+        if out is None:
+            out = torch.empty(inp.numel() // max(1, self.world_size), dtype=inp.dtype, device=inp.device)
+        self._check_collective(out, inp)
+        self._ops.reduce_scatter(self._ptr, inp, out)
+        if self.env.check:
+            torch.cuda.current_stream().synchronize()
+            self.check()
+        return out
+
+    def all_gather(self, inp: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """``out`` = every rank's ``inp`` concatenated in rank order."""
+        if out is None:
+            out = torch.empty(inp.numel() * self.world_size, dtype=inp.dtype, device=inp.device)
+        self._check_collective(inp, out)
+        self._ops.all_gather(self._ptr, inp, out)
         if self.env.check:
             torch.cuda.current_stream().synchronize()
             self.check()

@@ -5,6 +5,10 @@ so the schedule's plumbing (who sends which slice to whom, in which order the
 partial sums are added) is tested without a GPU. The result equals
 :func:`~numa_allreduce_b200.parallel.schedule.reference_allreduce` bit for bit
 and ``dist.all_reduce(SUM)`` to rounding.
+
+:func:`emulate_reduce_scatter` and :func:`emulate_all_gather` execute the
+contiguous-segment collectives the same way (segment j to its owner j, owner
+adds in rank order; own segment to every peer, concatenation in rank order).
 """
 
 from __future__ import annotations
@@ -82,3 +86,34 @@ def emulate_allreduce(tensor: torch.Tensor, schedule: HierSchedule, group=None) 
         pa, pb = sl[schedule.local_index(p)]
         out[pa:pb] = t
     return out.view(tensor.shape).to(tensor.device)
+
+
+def emulate_reduce_scatter(tensor: torch.Tensor, group=None) -> torch.Tensor:
+    """Reduce-scatter (SUM) over ``group``: ``tensor`` holds world_size equal
+    segments; this rank gets the sum of segment ``rank``, accumulated in fp32
+    in rank order and rounded once."""
+    rank = dist.get_rank(group)
+    ws = dist.get_world_size(group)
+    x = tensor.detach().reshape(-1).cpu().contiguous()
+    if x.numel() % ws:
+        raise ValueError("the input must hold world_size equal segments")
+    seg = x.numel() // ws
+    peers = [p for p in range(ws) if p != rank]
+    recv = _exchange({p: x[p * seg:(p + 1) * seg] for p in peers}, {p: (seg, x.dtype) for p in peers}, group)
+    acc = None
+    for q in range(ws):
+        part = x[rank * seg:(rank + 1) * seg] if q == rank else recv[q]
+        acc = part.float().clone() if acc is None else acc + part.float()
+    return acc.to(tensor.dtype).to(tensor.device)
+
+
+def emulate_all_gather(tensor: torch.Tensor, group=None) -> torch.Tensor:
+    """All-gather over ``group``: every rank's ``tensor`` (flattened) in rank
+    order."""
+    rank = dist.get_rank(group)
+    ws = dist.get_world_size(group)
+    x = tensor.detach().reshape(-1).cpu().contiguous()
+    peers = [p for p in range(ws) if p != rank]
+    recv = _exchange({p: x for p in peers}, {p: (x.numel(), x.dtype) for p in peers}, group)
+    parts = [x if q == rank else recv[q] for q in range(ws)]
+    return torch.cat(parts).to(tensor.device)

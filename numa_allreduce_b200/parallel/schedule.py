@@ -141,3 +141,28 @@ def reference_allreduce(inputs: list[torch.Tensor], schedule: HierSchedule) -> t
     for p in partials[1:]:
         acc = acc + p
     return acc.to(dtype)
+
+
+def reference_reduce_scatter(inputs: list[torch.Tensor]) -> list[torch.Tensor]:
+    """Exact result of the reduce-scatter collective: each input holds
+    ``world_size`` equal segments (flattened); rank r gets the fp32 sum of
+    segment r over the ranks in rank order, rounded once to the input dtype
+    (the matching slice of the one-shot allreduce's result, bit for bit)."""
+    ws = len(inputs)
+    flat = [x.reshape(-1) for x in inputs]
+    n = flat[0].numel()
+    if n % ws or any(f.numel() != n for f in flat):
+        raise ValueError("every input must hold world_size equal segments")
+    seg = n // ws
+    outs = []
+    for r in range(ws):
+        acc = flat[0][r * seg:(r + 1) * seg].float().clone()
+        for q in range(1, ws):
+            acc += flat[q][r * seg:(r + 1) * seg].float()
+        outs.append(acc.to(inputs[0].dtype))
+    return outs
+
+
+def reference_all_gather(inputs: list[torch.Tensor]) -> torch.Tensor:
+    """Exact result of the all-gather collective: the inputs in rank order."""
+    return torch.cat([x.reshape(-1) for x in inputs])

@@ -12,7 +12,8 @@ import pytest
 import torch
 
 from numa_allreduce_b200.ops.allreduce import EmulatedGroup
-from numa_allreduce_b200.parallel.schedule import HierSchedule, reference_allreduce
+from numa_allreduce_b200.parallel.schedule import (HierSchedule, reference_all_gather, reference_allreduce,
+                                                   reference_reduce_scatter)
 
 pytestmark = pytest.mark.gpu
 
@@ -148,3 +149,106 @@ def test_bad_arguments_raise():
             g.all_reduce(big, algo="oneshot")
         with pytest.raises((RuntimeError, ValueError)):
             g.all_reduce(x, algo="hier")  # no groups set
+
+
+@pytest.mark.parametrize("ws", [2, 3, 4, 8])
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_reduce_scatter_and_all_gather_bit_exact(ws, dtype):
+    """Segment collectives against the CPU oracle; segments longer than the
+    one-shot slot (64 KiB here) run as several launches, piece by piece."""
+    per_pack = 16 // torch.tensor([], dtype=dtype).element_size()
+    esz = torch.tensor([], dtype=dtype).element_size()
+    with EmulatedGroup(ws, oneshot_max=64 << 10) as g:
+        for seg in [per_pack, per_pack * 5, 4096 + per_pack * 3, (64 << 10) // esz, (200 << 10) // esz + per_pack]:
+            xs = _inputs(ws, ws * seg, dtype, seed=seg)
+            before = g.launches()
+            outs = g.reduce_scatter(xs)
+            torch.cuda.synchronize()
+            assert g.error_codes() == [0] * ws
+            pieces = -(-seg * esz // (64 << 10))
+            assert g.launches() - before == pieces * ws
+            ref = reference_reduce_scatter([x.cpu() for x in xs])
+            for r in range(ws):
+                assert torch.equal(outs[r].cpu(), ref[r]), f"reduce-scatter rank {r} segment {seg}"
+            mine = [x[:seg].contiguous() for x in xs]
+            gathered = g.all_gather(mine)
+            torch.cuda.synchronize()
+            assert g.error_codes() == [0] * ws
+            ref = reference_all_gather([m.cpu() for m in mine])
+            for r in range(ws):
+                assert torch.equal(gathered[r].cpu(), ref), f"all-gather rank {r} segment {seg}"
+
+
+def test_reduce_scatter_matches_allreduce_slice():
+    """Same arithmetic as the allreduce: bit-identical to its slice."""
+    ws = 4
+    with EmulatedGroup(ws) as g:
+        xs = _inputs(ws, ws * 8192, torch.bfloat16, seed=5)
+        full = g.all_reduce(xs, algo="oneshot")
+        parts = g.reduce_scatter(xs)
+        torch.cuda.synchronize()
+        for r in range(ws):
+            assert torch.equal(parts[r], full[0][r * 8192:(r + 1) * 8192])
+
+
+def test_collectives_interleaved_with_allreduce():
+    """Epochs and the shared one-shot slots across mixed call types."""
+    ws = 4
+    with EmulatedGroup(ws, chunk_max=16 << 10) as g:
+        for i in range(300):
+            n = [64, 4000 * 8, 8][i % 3]
+            xs = _inputs(ws, ws * n, torch.float16, seed=i)
+            kind = i % 3
+            if kind == 0:
+                outs = g.all_reduce(xs, algo=["oneshot", "twoshot", "twoshot_pipe"][i % 3 + (i // 3) % 2])
+                ref = reference_allreduce([x.cpu() for x in xs], HierSchedule.oneshot(ws))
+                if i % 30 == 0:
+                    assert all(torch.equal(o.cpu(), ref) for o in outs), i
+            elif kind == 1:
+                outs = g.reduce_scatter(xs)
+                if i % 30 == 1:
+                    ref = reference_reduce_scatter([x.cpu() for x in xs])
+                    assert all(torch.equal(outs[r].cpu(), ref[r]) for r in range(ws)), i
+            else:
+                mine = [x[:n].contiguous() for x in xs]
+                outs = g.all_gather(mine)
+                if i % 30 == 2:
+                    ref = reference_all_gather([m.cpu() for m in mine])
+                    assert all(torch.equal(o.cpu(), ref) for o in outs), i
+        torch.cuda.synchronize()
+        assert g.error_codes() == [0] * ws
+
+
+@pytest.mark.parametrize("kind", ["reduce_scatter", "all_gather"])
+def test_collective_absent_rank_times_out_and_recovers(kind):
+    ws = 4
+    with EmulatedGroup(ws, timeout_ns=200_000_000) as g:
+        xs = _inputs(ws, ws * 4096, torch.float32)
+        fn = getattr(g, kind)
+        args = xs if kind == "reduce_scatter" else [x[:4096].contiguous() for x in xs]
+        fn(args, participants=ws - 1)
+        torch.cuda.synchronize()  # returns: nothing hangs
+        assert g.error_codes()[0] == 1  # kErrTimeout
+        state = g.error_states()[0]
+        assert state[3] == (14 if kind == "reduce_scatter" else 15)  # the collective's stage tag
+        g.reset()
+        outs = fn(args)
+        torch.cuda.synchronize()
+        assert g.error_codes() == [0] * ws
+        if kind == "reduce_scatter":
+            assert torch.equal(outs[2].cpu(), reference_reduce_scatter([x.cpu() for x in xs])[2])
+        else:
+            assert torch.equal(outs[1].cpu(), reference_all_gather([a.cpu() for a in args]))
+
+
+def test_collective_bad_arguments_raise():
+    with EmulatedGroup(2) as g:
+        xs = [torch.zeros(2 * 12, device="cuda") for _ in range(2)]
+        g.reduce_scatter(xs)
+        with pytest.raises((RuntimeError, ValueError)):
+            g.reduce_scatter([torch.zeros(2 * 3, device="cuda") for _ in range(2)])  # 12-byte segments
+        with pytest.raises((RuntimeError, ValueError)):
+            g.all_gather([torch.zeros(8, device="cuda") for _ in range(2)],
+                         outs=[torch.zeros(8, device="cuda") for _ in range(2)])  # output too small
+        with pytest.raises((RuntimeError, ValueError)):
+            g.reduce_scatter(xs, outs=[x[:12] for x in xs])  # output aliases the input

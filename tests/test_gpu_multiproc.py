@@ -275,6 +275,60 @@ def _worker_llama(rank, ws, port):
     assert not errors, errors[:5]
 
 
+def _worker_collectives(rank, ws, port):
+    """reduce_scatter / all_gather across processes: bit-exact against the
+    rank-order oracle, equal to the matching slice of this library's
+    allreduce, and within rounding of NCCL's reduce_scatter_tensor (identical
+    to its all_gather_into_tensor)."""
+    from numa_allreduce_b200 import NumaAwareAllReduce, reference_all_gather, reference_reduce_scatter
+
+    _init(rank, ws, port)
+    errors = []
+    ar = None
+    try:
+        ar = NumaAwareAllReduce(dist.group.WORLD, device=rank)
+        for dtype in (torch.float32, torch.float16, torch.bfloat16):
+            esz = torch.tensor([], dtype=dtype).element_size()
+            for seg_bytes in (16, 4096 + 48, 1 << 20, (3 << 20) + 32):
+                seg = seg_bytes // esz
+                torch.manual_seed(100 + rank + seg)
+                x = torch.randn(ws * seg, dtype=dtype, device="cuda")
+                xs = _gather_cpu(x)
+                got = ar.reduce_scatter(x)
+                torch.cuda.synchronize()
+                ar.check()
+                if not torch.equal(got.cpu(), reference_reduce_scatter(xs)[rank]):
+                    errors.append(f"reduce_scatter {dtype} {seg_bytes} B: not bit-exact")
+                if seg_bytes <= (1 << 20) // ws:
+                    full = ar.all_reduce(x, algo="oneshot")
+                    torch.cuda.synchronize()
+                    if not torch.equal(got, full[rank * seg:(rank + 1) * seg]):
+                        errors.append(f"reduce_scatter {dtype} {seg_bytes} B: differs from the allreduce slice")
+                ref = torch.empty(seg, dtype=dtype, device="cuda")
+                dist.reduce_scatter_tensor(ref, x)
+                tol = 1e-5 if dtype == torch.float32 else 1e-2
+                if not torch.allclose(got.float(), ref.float(), rtol=tol, atol=tol * ws):
+                    errors.append(f"reduce_scatter {dtype} {seg_bytes} B: far from NCCL")
+                mine = x[:seg].contiguous()
+                gathered = ar.all_gather(mine)
+                torch.cuda.synchronize()
+                ar.check()
+                nccl = torch.empty(ws * seg, dtype=dtype, device="cuda")
+                dist.all_gather_into_tensor(nccl, mine)
+                if not torch.equal(gathered, nccl):
+                    errors.append(f"all_gather {dtype} {seg_bytes} B: differs from NCCL")
+                if not torch.equal(gathered.cpu(), reference_all_gather([t[:seg] for t in xs])):
+                    errors.append(f"all_gather {dtype} {seg_bytes} B: differs from the oracle")
+    except Exception as e:  # noqa: BLE001 - reported after the collective close
+        errors.append(repr(e))
+    finally:
+        torch.cuda.synchronize()
+        if ar is not None:
+            ar.close()
+        dist.destroy_process_group()
+    assert not errors, errors[:5]
+
+
 def _worker_reinit(rank, ws, port):
     """Repeated construction and close() in one process: every instance works
     and device memory returns to where it started (no leaked IPC buffers)."""
@@ -362,6 +416,12 @@ def _need(ws):
 def test_correctness_multiprocess(ws):
     _need(ws)
     mp.spawn(_worker_correctness, args=(ws, free_port()), nprocs=ws, join=True)
+
+
+@pytest.mark.parametrize("ws", [2, 4, 8])
+def test_reduce_scatter_all_gather(ws):
+    _need(ws)
+    mp.spawn(_worker_collectives, args=(ws, free_port()), nprocs=ws, join=True)
 
 
 @pytest.mark.parametrize("ws", [2, 8])

@@ -33,11 +33,15 @@ def test_c_abi_exports():
     for name in ("numa_all_reduce_init", "numa_all_reduce_dispose", "numa_all_reduce_register_buffer",
                  "numa_all_reduce_fp16", "numa_all_reduce_fp32", "numa_all_reduce_bf16", "nab_allreduce",
                  "nab_last_error", "nab_error_code", "nab_reset", "nab_set_auto_table", "nab_set_hybrid",
-                 "nab_auto_protocol"):
+                 "nab_auto_protocol", "nab_reduce_scatter", "nab_all_gather"):
         assert hasattr(lib, name)
     buf = ctypes.create_string_buffer(256)
     assert lib.nab_last_error(buf, 256) > 0  # message of the failed call above
     assert b"world size" in buf.value
+    assert lib.nab_reduce_scatter(None, None, None, None, ctypes.c_int64(8), 2) != 0
+    lib.nab_last_error(buf, 256)
+    assert b"null communicator" in buf.value
+    assert lib.nab_all_gather(None, None, None, None, ctypes.c_int64(8), 2) != 0
 
 
 @pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-GPU failure path")
