@@ -48,8 +48,9 @@ def parse():
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--single", action="store_true", help="emulate --ranks ranks on one GPU (ncu mode)")
     p.add_argument("--ranks", type=int, default=8)
-    p.add_argument("--op", default="allreduce", choices=["allreduce", "fused"],
-                   help="--single: the allreduce, or the fused allreduce + residual + RMSNorm")
+    p.add_argument("--op", default="allreduce", choices=["allreduce", "fused", "reduce_scatter", "all_gather"],
+                   help="--single: the allreduce, the fused allreduce + residual + RMSNorm, or a segment "
+                        "collective (--size-mb is then one rank's segment)")
     p.add_argument("--tokens", type=int, default=16, help="--op fused: rows T of the [T, hidden] message")
     p.add_argument("--hidden", type=int, default=8192, help="--op fused: hidden size H")
     p.add_argument("--groups", default=None, help="--single with --algo hier: e.g. 0,1,2,3|4,5,6,7")
@@ -77,6 +78,16 @@ def single_gpu(args):
 
             def call():
                 grp.all_reduce(ins, algo=algo, outs=outs)
+        elif args.op in ("reduce_scatter", "all_gather"):
+            seg = int(args.size_mb * (1 << 20)) // torch.tensor([], dtype=dt).element_size()
+            rs = args.op == "reduce_scatter"
+            ins = [torch.randn(seg * (args.ranks if rs else 1), device="cuda").to(dt) for _ in range(args.ranks)]
+            outs = [torch.empty(seg * (1 if rs else args.ranks), device="cuda", dtype=dt) for _ in range(args.ranks)]
+            nbytes = seg * ins[0].element_size()
+            algo = args.op
+
+            def call():
+                getattr(grp, args.op)(ins, outs=outs)
         else:
             T, H = args.tokens, args.hidden
             ins = [torch.randn(T, H, device="cuda").to(torch.bfloat16) for _ in range(args.ranks)]
