@@ -81,3 +81,33 @@ def test_gloo_collectives_match_oracle(ws, dtype_name):
         assert rs_err <= tol * ws, f"rank {rank}: reduce-scatter error {rs_err}"
         assert ag_exact, f"rank {rank}: all-gather differs"
         assert n_rs == seg and n_ag == ws * seg
+
+
+def _bare(ws):
+    """A NumaAwareAllReduce without a device: enough for the argument checks."""
+    from numa_allreduce_b200 import NumaAwareAllReduce
+
+    ar = object.__new__(NumaAwareAllReduce)
+    ar.disabled = False
+    ar.world_size = ws
+    return ar
+
+
+def test_collective_argument_checks():
+    ar = _bare(4)
+    seg = torch.zeros(8, dtype=torch.bfloat16)      # 16 bytes: the smallest valid segment
+    big = torch.zeros(32, dtype=torch.bfloat16)
+    ar._check_collective(seg, big)                   # fine
+    with pytest.raises(ValueError, match="world_size"):
+        ar._check_collective(seg, torch.zeros(24, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="16 bytes"):
+        ar._check_collective(torch.zeros(4, dtype=torch.bfloat16), torch.zeros(16, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="dtype"):
+        ar._check_collective(seg, big.float())
+    with pytest.raises(ValueError, match="dtype"):
+        ar._check_collective(seg.to(torch.int16), big.to(torch.int16))
+    with pytest.raises(ValueError, match="contiguous"):
+        ar._check_collective(torch.zeros(16, dtype=torch.bfloat16)[::2], big)
+    ar.disabled = True
+    with pytest.raises(RuntimeError, match="disabled"):
+        ar._check_collective(seg, big)
