@@ -12,6 +12,9 @@ reads. Every variable below is actually read:
                            ``hybrid``, ``hier``, ``pull``, ``nccl`` or ``auto``
                            (default)
 ``NAB_MAX_SIZE``           largest message (bytes) the custom path takes
+``NAB_COLLECTIVE_MAX``     largest segment (bytes per rank) that
+                           ``custom_reduce_scatter`` / ``custom_all_gather``
+                           take (default 1 MiB); larger ones return None
 ``NAB_TIMEOUT_NS``         bound of every device-side wait (default 5 s)
 ``NAB_TUNING_FILE``        JSON table of protocol thresholds (see select.py)
 ``NAB_LOG_LEVEL``          logging level name (default WARNING)
@@ -84,6 +87,7 @@ class EnvConfig:
     disable: bool = False
     algo: str = "auto"
     max_size: int | None = None
+    collective_max: int = 1 << 20
     timeout_ns: int = 5_000_000_000
     tuning_file: str | None = None
     log_level: str = "WARNING"
@@ -107,6 +111,7 @@ def read_env() -> EnvConfig:
         disable=_flag("NAB_DISABLE"),
         algo=algo,
         max_size=_int("NAB_MAX_SIZE", None),
+        collective_max=_int("NAB_COLLECTIVE_MAX", 1 << 20),
         timeout_ns=_int("NAB_TIMEOUT_NS", 5_000_000_000),
         tuning_file=os.environ.get("NAB_TUNING_FILE"),
         log_level=os.environ.get("NAB_LOG_LEVEL", "WARNING"),

@@ -111,3 +111,33 @@ def test_collective_argument_checks():
     ar.disabled = True
     with pytest.raises(RuntimeError, match="disabled"):
         ar._check_collective(seg, big)
+
+
+def test_custom_collectives_hand_large_or_odd_messages_to_nccl(monkeypatch):
+    """custom_reduce_scatter / custom_all_gather return None ("use NCCL") above
+    the segment cap and for inputs the kernel cannot take; otherwise they run
+    the collective (stubbed here: no GPU)."""
+    from numa_allreduce_b200.utils.env import read_env
+
+    ar = _bare(4)
+    ar.env = read_env()
+    assert ar.env.collective_max == 1 << 20
+    calls = []
+    monkeypatch.setattr(type(ar), "reduce_scatter", lambda self, x, out=None: calls.append(("rs", x.numel())) or x)
+    monkeypatch.setattr(type(ar), "all_gather", lambda self, x, out=None: calls.append(("ag", x.numel())) or x)
+    bf = torch.bfloat16
+    assert ar.custom_reduce_scatter(torch.zeros(4 * 8, dtype=bf)) is not None           # 16-byte segments
+    assert ar.custom_reduce_scatter(torch.zeros(4 * (1 << 19), dtype=bf)) is not None   # 1 MiB segments
+    assert ar.custom_reduce_scatter(torch.zeros(4 * (1 << 19) + 32, dtype=bf)) is None  # above the cap
+    assert ar.custom_reduce_scatter(torch.zeros(30, dtype=bf)) is None                  # not 4 segments
+    assert ar.custom_reduce_scatter(torch.zeros(4 * 4, dtype=bf)) is None               # 8-byte segments
+    assert ar.custom_reduce_scatter(torch.zeros(64, dtype=torch.int32)) is None         # dtype
+    assert ar.custom_reduce_scatter(torch.zeros(128, dtype=bf)[::2]) is None            # not contiguous
+    assert ar.custom_all_gather(torch.zeros(1 << 19, dtype=bf)) is not None
+    assert ar.custom_all_gather(torch.zeros((1 << 19) + 8, dtype=bf)) is None
+    assert calls == [("rs", 32), ("rs", 4 << 19), ("ag", 1 << 19)]
+    monkeypatch.setenv("NAB_COLLECTIVE_MAX", str(64 << 20))
+    ar.env = read_env()
+    assert ar.custom_reduce_scatter(torch.zeros(4 * (1 << 20), dtype=bf)) is not None
+    ar.disabled = True
+    assert ar.custom_all_gather(torch.zeros(8, dtype=bf)) is None
