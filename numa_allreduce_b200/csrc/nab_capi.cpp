@@ -10,6 +10,7 @@
 // workspaces (nab_workspace_bytes(world_size) bytes each, zero-initialised,
 // IPC-mapped), and `nnuma` splits the ranks into that many contiguous groups
 // for the hierarchical protocol, as the reference's build_numa_mappings did.
+// C declarations: nab_capi.h.
 #include <cuda_runtime.h>
 
 #include <cstring>
@@ -18,6 +19,7 @@
 #include <string>
 #include <vector>
 
+#include "nab_capi.h"
 #include "nab_comm.h"
 
 #define NAB_API extern "C" __attribute__((visibility("default")))

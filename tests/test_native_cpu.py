@@ -1,6 +1,8 @@
 """The native library builds for sm_100a and loads on a host without a GPU."""
 
 import ctypes
+import os
+from pathlib import Path
 
 import pytest
 import torch
@@ -51,3 +53,39 @@ def test_c_abi_init_fails_cleanly_without_gpu():
     ptrs = (ctypes.c_void_p * 2)(4096, 8192)
     h = lib.numa_all_reduce_init(ptrs, None, 0, 0, 2, 1)
     assert h is None
+
+
+def test_c_header_compiles_and_links(tmp_path):
+    """A C program that includes nab_capi.h and nab_noalloc.h compiles as C11
+    and links against libnab.so: the headers declare what the library
+    exports."""
+    import shutil
+    import subprocess
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    _ext.load()
+    csrc = Path(_ext.plain_library_path()).parent / "csrc"
+    cuda_inc = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda")) / "include"
+    prog = tmp_path / "use_abi.c"
+    prog.write_text(
+        '#include "nab_capi.h"\n#include "nab_noalloc.h"\n#include <stdio.h>\n'
+        "int main(void) {\n"
+        "  char buf[128];\n"
+        "  int64_t ws = nab_workspace_bytes(8);\n"
+        "  int bad = nab_workspace_bytes(9) == -1 && nab_last_error(buf, sizeof buf) > 0;\n"
+        "  void* fns[] = {(void*)numa_all_reduce_init, (void*)numa_all_reduce_dispose,\n"
+        "    (void*)numa_all_reduce_register_buffer, (void*)numa_all_reduce_fp16, (void*)numa_all_reduce_fp32,\n"
+        "    (void*)numa_all_reduce_bf16, (void*)nab_allreduce, (void*)nab_reduce_scatter, (void*)nab_all_gather,\n"
+        "    (void*)nab_set_auto_table, (void*)nab_set_hybrid, (void*)nab_auto_protocol, (void*)nab_error_code,\n"
+        "    (void*)nab_reset, (void*)nab_noalloc_emulated_allreduce, (void*)nab_noalloc_last_error};\n"
+        "  for (unsigned i = 0; i < sizeof fns / sizeof fns[0]; ++i) if (!fns[i]) return 2;\n"
+        '  printf("%lld %d\\n", (long long)ws, bad);\n'
+        "  return ws > 0 && bad ? 0 : 1;\n}\n")
+    lib = Path(_ext.plain_library_path())
+    exe = tmp_path / "use_abi"
+    subprocess.run([cc, "-std=c11", "-Wall", "-Werror", f"-I{csrc}", f"-I{cuda_inc}", str(prog), "-o", str(exe),
+                    f"-L{lib.parent}", "-lnab", f"-Wl,-rpath,{lib.parent}"], check=True)
+    r = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout + r.stderr
